@@ -1,0 +1,269 @@
+/*
+ * lmpb.h — C ABI of the Lamp3 B200 backend (sm_100a).
+ *
+ * This is the flat kernel layer that sits under Lamp3's CUDA dispatch.  Every
+ * entry point takes plain device pointers, element counts and shapes, and a
+ * cudaStream_t passed as `void*` (NULL = the legacy default stream).  No entry
+ * point allocates an OUTPUT: the caller owns every input and output buffer,
+ * exactly as the reference's `TensorMetaHandler` allocates the output before
+ * the kernel runs (csrc/src/tensor/cpu/meta_handler.cpp:9-73).  Kernels are
+ * launched asynchronously on the given stream; a host read must synchronise
+ * that stream first.
+ *
+ * Each function names the reference interface it replaces (paths are relative
+ * to the rushlite project root).  The reference registers one function pointer
+ * per op and device in a `DispatchStub` table
+ * (csrc/include/lamp3/tensor/dispatch_stub.hpp:21-64); a CUDA registration
+ * unit built on this header wraps each stub signature around one call here
+ * (the shim is shown in INTEGRATION.md).
+ *
+ * Errors: every call returns an lmpb_status.  LMPB_ERR_INVALID mirrors the
+ * reference's user-error LMP_CHECK (a throw of std::runtime_error,
+ * csrc/include/lamp3/common/assert.hpp:89-90); the other codes replace
+ * LMP_CUDA_CHECK's std::terminate (assert.hpp:95-102) by a status the caller
+ * can turn into an exception.  lmpb_last_error() returns the calling thread's
+ * message for its last failed call.
+ */
+#ifndef LMPB_H_
+#define LMPB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LMPB_MAX_DIMS 16 /* csrc/include/lamp3/tensor/utils/align_utils.hpp:7 */
+
+/* Element types, same numbering as lmp::tensor::DataType
+ * (csrc/include/lamp3/tensor/data_type.hpp:25-32).  The output type of a
+ * binary op is the larger enum value (type_upcast, data_type.hpp:77-80). */
+typedef enum {
+  LMPB_BOOL = 0,
+  LMPB_INT16 = 1,
+  LMPB_INT32 = 2,
+  LMPB_INT64 = 3,
+  LMPB_FLOAT32 = 4,
+  LMPB_FLOAT64 = 5
+} lmpb_dtype;
+
+typedef enum {
+  LMPB_OK = 0,
+  LMPB_ERR_INVALID = 1,     /* bad argument: shape, dtype, op, null pointer */
+  LMPB_ERR_CUDA = 2,        /* a CUDA runtime / driver call failed */
+  LMPB_ERR_UNSUPPORTED = 3, /* valid request this build does not serve */
+  LMPB_ERR_COMPILE = 4,     /* NVRTC rejected a generated fused kernel */
+  LMPB_ERR_TIMEOUT = 5      /* a bounded device wait gave up */
+} lmpb_status;
+
+/* Binary ops: ops::add..lt (csrc/src/tensor/native/expand_ops.cpp:28-160),
+ * functors csrc/include/lamp3/tensor/cpu/kernels.hpp:22-64.  Comparisons
+ * produce 1/0 in the output dtype (not bool). */
+typedef enum {
+  LMPB_ADD = 0,
+  LMPB_SUB = 1,
+  LMPB_MUL = 2,
+  LMPB_DIV = 3,
+  LMPB_POW = 4,
+  LMPB_EQ = 5,
+  LMPB_NE = 6,
+  LMPB_GE = 7,
+  LMPB_LE = 8,
+  LMPB_GT = 9,
+  LMPB_LT = 10,
+  /* the two same-shape backward kernels, unary_ops.hpp:103-105 */
+  LMPB_ABS_BACKWARD = 11,
+  LMPB_CLAMP_BACKWARD = 12
+} lmpb_binary_op;
+
+/* Unary ops: ops::neg..tan, clamp (csrc/src/tensor/native/unary_ops.cpp:23-55) */
+typedef enum {
+  LMPB_NEG = 0,
+  LMPB_EXP = 1,
+  LMPB_LOG = 2,
+  LMPB_SQRT = 3,
+  LMPB_ABS = 4,
+  LMPB_SIN = 5,
+  LMPB_COS = 6,
+  LMPB_TAN = 7,
+  LMPB_CLAMP = 8
+} lmpb_unary_op;
+
+/* Reductions: ops::sum/max/min/prod (csrc/src/tensor/native/reduct_ops.cpp:12-28) */
+typedef enum { LMPB_SUM = 0, LMPB_MAX = 1, LMPB_MIN = 2, LMPB_PROD = 3 } lmpb_reduce_op;
+
+/* Copy directions for lmpb_copy. */
+typedef enum { LMPB_H2D = 0, LMPB_D2H = 1, LMPB_D2D = 2, LMPB_H2H = 3 } lmpb_copy_kind;
+
+/* ---------------------------------------------------------------- errors */
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* lmpb_last_error(void);
+/* Library version string; also proves the library loaded. */
+const char* lmpb_version(void);
+
+/* ------------------------------------------------------------ shapes */
+
+/* NumPy broadcast of two shapes (AlignUtil::calc_aligned_shape,
+ * csrc/src/tensor/utils/align_utils.cpp:18-40).  Writes out_shape (room for
+ * LMPB_MAX_DIMS) and *out_ndim; LMPB_ERR_INVALID on a broadcast violation. */
+lmpb_status lmpb_broadcast_shape(const int64_t* a_shape, int a_ndim, const int64_t* b_shape,
+                                 int b_ndim, int64_t* out_shape, int* out_ndim);
+
+/* ------------------------------------------------------- elementwise */
+
+/* out = op(a, b) with NumPy broadcasting of row-major contiguous a and b.
+ * Replaces add_cuda..lt_cuda (csrc/src/tensor/cuda/kernels.cu:13-64) and the
+ * binary/expand dispatch handlers behind them (cuda/binary.cu:63-96,
+ * cuda/expand.cu:38-59).  Both operands are converted to out_dtype before
+ * the op (cuda/ptr_pack.cuh:12-17); out_dtype is normally
+ * max(a_dtype, b_dtype).  `out` holds prod(broadcast shape) elements.
+ * LMPB_ABS_BACKWARD / LMPB_CLAMP_BACKWARD take (input, grad) as (a, b) and
+ * need equal shapes and dtypes (abs_backward_cuda / clamp_backward_cuda,
+ * csrc/src/tensor/native/unary_ops.cpp:57-83); p0/p1 are clamp's min/max. */
+lmpb_status lmpb_binary(int op, int out_dtype, const void* a, int a_dtype, const int64_t* a_shape,
+                        int a_ndim, const void* b, int b_dtype, const int64_t* b_shape, int b_ndim,
+                        void* out, double p0, double p1, void* stream);
+
+/* out[i] = op(in[i]) for n elements, out and in of the same dtype
+ * (infer_unary, csrc/src/tensor/infer_meta.cpp:11-17).  Replaces
+ * neg_cuda..clamp_cuda (csrc/src/tensor/cuda/kernels.cu:31-64; cuda/unary.cu:13-82).
+ * Integer inputs of exp/log/sqrt/sin/cos/tan compute in double and truncate
+ * (cuda/kernels.cuh:24-25).  p0/p1 are clamp's min/max (ignored otherwise). */
+lmpb_status lmpb_unary(int op, int dtype, const void* in, void* out, int64_t n, double p0,
+                       double p1, void* stream);
+
+/* ------------------------------------------------------- reductions */
+
+/* Keep-dim reduction of row-major `in` (shape[ndim]) along `axis` into `out`
+ * (shape with shape[axis] = 1), accumulating in the input dtype
+ * (infer_reduct, csrc/src/tensor/infer_meta.cpp:35-44).  Replaces
+ * sum_cuda..prod_cuda (csrc/src/tensor/cuda/kernels.cu:112-122) and
+ * reduct_dispatch_handler (cuda/reduct.cu:213-260).  Integer sums, max and min
+ * are bit-exact with the reference; float sums and products differ only by
+ * summation order.  Results are deterministic run to run.  A large reduction
+ * over a leading axis uses a split workspace that the library takes from
+ * CUDA's stream-ordered pool (cudaMallocAsync) on `stream`. */
+lmpb_status lmpb_reduce(int op, int dtype, const void* in, const int64_t* shape, int ndim,
+                        int axis, void* out, void* stream);
+
+/* ----------------------------------------------------------- matmul */
+
+/* C[m,n] = A[m,k] · B[k,n], row-major, converted to out_dtype
+ * (matmul_cuda, csrc/src/tensor/cuda/kernels.cu:83-110; cuda/matrix.cu:178-199).
+ * fp32 × fp32 → fp32 runs on the tcgen05 tensor cores as 3xTF32 (hi·hi + hi·lo
+ * + lo·hi, fp32 accumulate in TMEM); other dtype combinations use a SIMT
+ * kernel that accumulates in out_dtype like the reference. */
+lmpb_status lmpb_matmul(int out_dtype, const void* A, int a_dtype, const void* B, int b_dtype,
+                        void* C, int64_t m, int64_t k, int64_t n, void* stream);
+
+/* fp32 GEMM with operand transposes and accumulate, on the same 3xTF32
+ * tensor-core path:  C[m,n] = op(A)·op(B) + beta·C, op(X) = X or Xᵀ of a
+ * row-major array (A is [m,k] or, with trans_a, [k,m]; B is [k,n] or, with
+ * trans_b, [n,k]).  beta is 0 or 1.  This lets autograd compute
+ * dA = G·Bᵀ and dB = Aᵀ·G and accumulate them into the grad buffers without
+ * materialising the transposes that MatrixMultiplicationBackward builds
+ * (csrc/src/autograd/functions/matrix_ops.cpp:8-24). */
+lmpb_status lmpb_gemm_f32(int trans_a, int trans_b, const float* A, const float* B, float* C,
+                          int64_t m, int64_t n, int64_t k, float beta, void* stream);
+
+/* out[n,m] = in[m,n]ᵀ (transpose_cuda, csrc/src/tensor/cuda/kernels.cu:66-81). */
+lmpb_status lmpb_transpose(int dtype, const void* in, void* out, int64_t m, int64_t n,
+                           void* stream);
+
+/* ----------------------------------------------------------- memory */
+
+/* Device allocation from CUDA's stream-ordered pool; replaces empty_cuda and
+ * the caching allocator (csrc/src/tensor/cuda/memory.cu:56-65,
+ * cuda/allocator.cu:39-138).  Blocks are 256-byte aligned.  These are the
+ * only calls that allocate, and a caller with its own allocator can skip them. */
+lmpb_status lmpb_malloc(void** ptr, size_t bytes, void* stream);
+lmpb_status lmpb_free(void* ptr, void* stream);
+
+/* fill_cuda (csrc/src/tensor/cuda/memory.cu:67-73): ptr[0..n) = (T)value. */
+lmpb_status lmpb_fill(int dtype, void* ptr, int64_t n, double value, void* stream);
+
+/* copy_cuda (csrc/src/tensor/cuda/memory.cu:126-174): casting copy of n
+ * elements between host and device.  A host side must stay valid until the
+ * stream reaches the copy (pinned memory makes it asynchronous). */
+lmpb_status lmpb_copy(int kind, const void* src, int src_dtype, void* dst, int dst_dtype,
+                      int64_t n, void* stream);
+
+/* add_inplace_cuda (csrc/src/tensor/cuda/memory.cu:22-83): dst[i] += src[i],
+ * the gradient accumulation of Variable::incr_grad
+ * (csrc/src/autograd/variable.cpp:30-35). */
+lmpb_status lmpb_add_inplace(int dtype, void* dst, const void* src, int64_t n, void* stream);
+
+/* ------------------------------------------------------ fused kernels */
+
+/* The lazy-fusion compiler behind capture_on / capture.  Replaces the NVRTC
+ * inductor (build_fused_graph csrc/src/inductor/nvrtc/fused_graph.cpp:6-35,
+ * codegen_kernel codegen.cpp:21-61, NVRTCInductorBackend::realize
+ * nvrtc_backend.cpp:145-190).  Unlike the reference, a fused region may
+ * contain broadcast leaves, constant fills, and reductions of its result over
+ * broadcast axes, and may write several outputs from one pass.
+ *
+ * A program is a DAG of lmpb_fnode in topological order over one iteration
+ * space `iter_shape`.  Leaves are device arrays whose shapes broadcast to the
+ * iteration space.  Every node computes in its own dtype after converting its
+ * inputs to that dtype (codegen.cpp:45-55).  Each output names a node and a
+ * mode: STORE writes the full iteration space, ACCUM adds into an existing
+ * full-size buffer (add_inplace fused in), REDUCE_SUM / REDUCE_SUM_ACCUM sum
+ * the node over the axes where out_shape is 1 (the sum_broadcast_axis of
+ * csrc/src/autograd/utils/grad_utils.cpp:10-36) and store or accumulate. */
+typedef enum {
+  LMPB_FN_LEAF = 0,   /* reads leaf slot `a` */
+  LMPB_FN_CONST = 1,  /* the constant p0 */
+  LMPB_FN_BINARY = 2, /* binary op `sub` on nodes a, b (params p0/p1 for clamp_backward) */
+  LMPB_FN_UNARY = 3   /* unary op `sub` on node a (p0/p1 for clamp) */
+} lmpb_fnode_kind;
+
+typedef struct {
+  int32_t kind;  /* lmpb_fnode_kind */
+  int32_t sub;   /* lmpb_binary_op / lmpb_unary_op */
+  int32_t dtype; /* lmpb_dtype the node computes in */
+  int32_t a, b;  /* input node indices (or leaf slot for LEAF) */
+  double p0, p1;
+} lmpb_fnode;
+
+typedef struct {
+  int32_t dtype;
+  int32_t ndim;
+  int64_t shape[LMPB_MAX_DIMS]; /* right-aligned broadcast to the iteration space */
+} lmpb_fleaf;
+
+typedef enum {
+  LMPB_OUT_STORE = 0,
+  LMPB_OUT_ACCUM = 1,
+  LMPB_OUT_REDUCE_SUM = 2,
+  LMPB_OUT_REDUCE_SUM_ACCUM = 3
+} lmpb_fout_mode;
+
+typedef struct {
+  int32_t node;
+  int32_t mode;  /* lmpb_fout_mode */
+  int32_t dtype; /* dtype of the output buffer */
+  int32_t ndim;
+  int64_t shape[LMPB_MAX_DIMS]; /* == iter shape, or with 1s on reduced axes */
+} lmpb_fout;
+
+typedef struct lmpb_fused_s* lmpb_fused;
+
+/* Compile (or fetch from the in-process and on-disk caches) a fused kernel.
+ * The handle is valid until lmpb_fused_release. */
+lmpb_status lmpb_fused_build(const lmpb_fnode* nodes, int n_nodes, const lmpb_fleaf* leaves,
+                             int n_leaves, const lmpb_fout* outs, int n_outs,
+                             const int64_t* iter_shape, int iter_ndim, lmpb_fused* handle);
+/* Launch it: leaf_ptrs[n_leaves] inputs, out_ptrs[n_outs] outputs. */
+lmpb_status lmpb_fused_launch(lmpb_fused handle, const void* const* leaf_ptrs,
+                              void* const* out_ptrs, void* stream);
+lmpb_status lmpb_fused_release(lmpb_fused handle);
+/* Generated CUDA source of a handle (for tests and debugging). */
+const char* lmpb_fused_source(lmpb_fused handle);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LMPB_H_ */

@@ -1,0 +1,350 @@
+// Keep-dim reductions (sum / max / min / prod) along one axis.
+//
+// The input is viewed as [outer, R, inner] with R the reduced extent.
+//  * inner == 1 (last axis): each row is reduced by one CTA (long rows) or
+//    one warp (short rows) with 16-byte vector loads and a warp-shuffle tree.
+//  * inner  > 1 (leading / middle axis): a thread owns a 16-byte vector of
+//    adjacent columns and walks down the R rows, so every warp load is a
+//    fully coalesced 512-byte segment.  When outer x column-blocks cannot fill
+//    the 148 SMs, R is split into S chunks whose partials go to a workspace
+//    and a second kernel combines them in chunk order.  No float atomics, so
+//    results are identical run to run.
+// Accumulation stays in the input dtype (the reference's functors are
+// instantiated on the output type, csrc/src/tensor/cpu/reduct.cpp:33-49),
+// which keeps int32 sums, max and min bit-exact with the reference; a float
+// sum differs from the reference's sequential order only by rounding.
+#include <limits>
+
+#include "common.cuh"
+
+namespace lmpb {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int OP, typename T>
+struct RedOp {
+  static __host__ __device__ __forceinline__ T identity() {
+    if constexpr (OP == LMPB_SUM) return T(0);
+    else if constexpr (OP == LMPB_PROD) return T(1);
+    else if constexpr (OP == LMPB_MAX) return std::numeric_limits<T>::lowest();
+    else return std::numeric_limits<T>::max();
+  }
+  // `acc` covers lower indices than `x`; max/min keep `acc` on ties like
+  // std::max / std::min in the reference's sequential loop.
+  static __device__ __forceinline__ T apply(T acc, T x) {
+    if constexpr (OP == LMPB_SUM) return static_cast<T>(r_add(acc, x));
+    else if constexpr (OP == LMPB_PROD) return static_cast<T>(r_mul(acc, x));
+    else if constexpr (OP == LMPB_MAX) return (acc < x) ? x : acc;
+    else return (x < acc) ? x : acc;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ T shfl_down(T v, int delta) {
+  if constexpr (sizeof(T) < 4) {
+    int t = static_cast<int>(v);
+    return static_cast<T>(__shfl_down_sync(0xffffffffu, t, delta));
+  } else {
+    return __shfl_down_sync(0xffffffffu, v, delta);
+  }
+}
+
+template <int OP, typename T>
+__device__ __forceinline__ T warp_reduce(T v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = RedOp<OP, T>::apply(v, shfl_down(v, d));
+  return v;
+}
+
+template <typename T>
+struct V16 {
+  static constexpr int N = 16 / sizeof(T);
+  union {
+    uint4 raw;
+    T v[N];
+  };
+};
+
+// Reduces `len` contiguous elements starting at `row` with the threads
+// [lane0, lane0 + nthreads); returns the per-thread partial.
+template <int OP, typename T, bool VEC>
+__device__ __forceinline__ T row_partial(const T* __restrict__ row, int64_t len, int tid,
+                                         int nthreads) {
+  using R = RedOp<OP, T>;
+  T acc = R::identity();
+  if constexpr (VEC) {
+    constexpr int N = V16<T>::N;
+    const uint4* r4 = reinterpret_cast<const uint4*>(row);
+    const int64_t nv = len / N;
+    int64_t i = tid;
+    for (; i + 3 * nthreads < nv; i += 4 * nthreads) {
+      V16<T> x0, x1, x2, x3;
+      x0.raw = __ldg(r4 + i);
+      x1.raw = __ldg(r4 + i + nthreads);
+      x2.raw = __ldg(r4 + i + 2 * nthreads);
+      x3.raw = __ldg(r4 + i + 3 * nthreads);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc = R::apply(acc, x0.v[j]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc = R::apply(acc, x1.v[j]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc = R::apply(acc, x2.v[j]);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc = R::apply(acc, x3.v[j]);
+    }
+    for (; i < nv; i += nthreads) {
+      V16<T> x;
+      x.raw = __ldg(r4 + i);
+#pragma unroll
+      for (int j = 0; j < N; ++j) acc = R::apply(acc, x.v[j]);
+    }
+    for (int64_t t = nv * N + tid; t < len; t += nthreads) acc = R::apply(acc, row[t]);
+  } else {
+    for (int64_t t = tid; t < len; t += nthreads) acc = R::apply(acc, row[t]);
+  }
+  return acc;
+}
+
+// One CTA per row (grid-stride over rows).
+template <int OP, typename T, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    reduce_rows_cta_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t rows,
+                           int64_t len) {
+  __shared__ T warp_part[kThreads / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    T acc = row_partial<OP, T, VEC>(in + r * len, len, threadIdx.x, kThreads);
+    acc = warp_reduce<OP, T>(acc);
+    if (lane == 0) warp_part[wid] = acc;
+    __syncthreads();
+    if (wid == 0) {
+      T v = lane < kThreads / 32 ? warp_part[lane] : RedOp<OP, T>::identity();
+      v = warp_reduce<OP, T>(v);
+      if (lane == 0) out[r] = v;
+    }
+    __syncthreads();
+  }
+}
+
+// One warp per row.
+template <int OP, typename T, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    reduce_rows_warp_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t rows,
+                            int64_t len) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
+  for (int64_t r = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); r < rows;
+       r += warps) {
+    T acc = row_partial<OP, T, VEC>(in + r * len, len, lane, 32);
+    acc = warp_reduce<OP, T>(acc);
+    if (lane == 0) out[r] = acc;
+  }
+}
+
+// Column reduction of [outer, R, inner]: thread owns VW adjacent columns of
+// one outer slice and rows [r0, r1) of chunk blockIdx.z; writes the partial
+// to dst[(chunk * outer + o) * inner + c].
+template <int OP, typename T, int VW>
+__global__ void __launch_bounds__(kThreads)
+    reduce_cols_kernel(const T* __restrict__ in, T* __restrict__ dst, int64_t outer, int64_t R,
+                       int64_t inner, int64_t rows_per_chunk) {
+  using Rd = RedOp<OP, T>;
+  const int64_t cvec = (int64_t)blockIdx.x * kThreads + threadIdx.x;  // vector column index
+  const int64_t c = cvec * VW;
+  const int64_t o = blockIdx.y;
+  const int64_t chunk = blockIdx.z;
+  if (c >= inner) return;
+  const int64_t r0 = chunk * rows_per_chunk;
+  int64_t r1 = r0 + rows_per_chunk;
+  if (r1 > R) r1 = R;
+  const T* base = in + (o * R) * inner + c;
+  T acc[VW];
+#pragma unroll
+  for (int j = 0; j < VW; ++j) acc[j] = Rd::identity();
+  if constexpr (VW > 1) {
+    int64_t r = r0;
+    for (; r + 3 < r1; r += 4) {
+      V16<T> x0, x1, x2, x3;
+      x0.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 0) * inner));
+      x1.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 1) * inner));
+      x2.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 2) * inner));
+      x3.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 3) * inner));
+#pragma unroll
+      for (int j = 0; j < VW; ++j) {
+        acc[j] = Rd::apply(acc[j], x0.v[j]);
+        acc[j] = Rd::apply(acc[j], x1.v[j]);
+        acc[j] = Rd::apply(acc[j], x2.v[j]);
+        acc[j] = Rd::apply(acc[j], x3.v[j]);
+      }
+    }
+    for (; r < r1; ++r) {
+      V16<T> x;
+      x.raw = __ldg(reinterpret_cast<const uint4*>(base + r * inner));
+#pragma unroll
+      for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x.v[j]);
+    }
+    V16<T> res;
+#pragma unroll
+    for (int j = 0; j < VW; ++j) res.v[j] = acc[j];
+    *reinterpret_cast<uint4*>(dst + (chunk * outer + o) * inner + c) = res.raw;
+  } else {
+    for (int64_t r = r0; r < r1; ++r) acc[0] = Rd::apply(acc[0], base[r * inner]);
+    dst[(chunk * outer + o) * inner + c] = acc[0];
+  }
+}
+
+// Combines S chunk partials in chunk order: out[i] = op over s of part[s][i].
+template <int OP, typename T>
+__global__ void __launch_bounds__(kThreads)
+    reduce_combine_kernel(const T* __restrict__ part, T* __restrict__ out, int64_t n, int S) {
+  using Rd = RedOp<OP, T>;
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * kThreads) {
+    T acc = part[i];
+    for (int s = 1; s < S; ++s) acc = Rd::apply(acc, part[(int64_t)s * n + i]);
+    out[i] = acc;
+  }
+}
+
+template <int OP, typename T>
+__global__ void fill_identity_kernel(T* out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = RedOp<OP, T>::identity();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename T>
+int64_t pick_chunks(int64_t outer, int64_t R, int64_t inner, int vw) {
+  const int64_t colblocks = (inner / vw + kThreads - 1) / kThreads;
+  const int64_t ctas = colblocks * outer;
+  const int64_t target = (int64_t)sm_count() * 4;
+  if (ctas >= target || R < 64) return 1;
+  int64_t S = (target + ctas - 1) / ctas;
+  if (S > R / 16) S = R / 16;  // keep >= 16 rows per chunk
+  if (S < 1) S = 1;
+  return S;
+}
+
+}  // namespace
+
+// Reduction plan shared by the allocating and workspace-taking entry points.
+struct ReducePlan {
+  int64_t outer, R, inner;
+  int64_t S;  // chunks (1 = no workspace)
+  int vw;     // column vector width
+  size_t ws_bytes;
+};
+
+template <typename T>
+static ReducePlan plan_reduce(const void* in, const void* out, int64_t outer, int64_t R, int64_t inner) {
+  ReducePlan p{outer, R, inner, 1, 1, 0};
+  if (inner > 1) {
+    constexpr int N = V16<T>::N;
+    p.vw = (inner % N == 0 && aligned16(in) && aligned16(out)) ? N : 1;
+    p.S = pick_chunks<T>(outer, R, inner, p.vw);
+    if (p.S > 1) p.ws_bytes = (size_t)p.S * outer * inner * sizeof(T);
+  }
+  return p;
+}
+
+template <int OP, typename T>
+static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, cudaStream_t st) {
+  const int64_t nout = p.outer * p.inner;
+  if (p.R == 0) {
+    fill_identity_kernel<OP, T><<<(int)std::min<int64_t>((nout + 255) / 256, 4096), 256, 0, st>>>(out, nout);
+    return launch_status("fill_identity_kernel");
+  }
+  if (p.inner == 1) {
+    constexpr int N = V16<T>::N;
+    const bool vec = (p.R % N == 0) && aligned16(in);
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (p.R >= 2048) {
+      int grid = (int)std::min<int64_t>(p.outer, cap);
+      if (vec) reduce_rows_cta_kernel<OP, T, true><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+      else reduce_rows_cta_kernel<OP, T, false><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+    } else {
+      int grid = (int)std::min<int64_t>((p.outer + 7) / 8, cap);
+      if (vec) reduce_rows_warp_kernel<OP, T, true><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+      else reduce_rows_warp_kernel<OP, T, false><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+    }
+    return launch_status("reduce_rows_kernel");
+  }
+  constexpr int N = V16<T>::N;
+  const int64_t colblocks = (p.inner / p.vw + kThreads - 1) / kThreads;
+  const int64_t rows_per_chunk = (p.R + p.S - 1) / p.S;
+  if (p.outer > 65535 || p.S > 65535)
+    return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce: outer extent too large for the column kernel");
+  dim3 grid((unsigned)colblocks, (unsigned)p.outer, (unsigned)p.S);
+  T* dst = p.S > 1 ? ws : out;
+  if (p.vw == N)
+    reduce_cols_kernel<OP, T, N><<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
+  else
+    reduce_cols_kernel<OP, T, 1><<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
+  lmpb_status s = launch_status("reduce_cols_kernel");
+  if (s != LMPB_OK || p.S == 1) return s;
+  int g2 = (int)std::min<int64_t>((nout + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
+  reduce_combine_kernel<OP, T><<<g2, kThreads, 0, st>>>(ws, out, nout, (int)p.S);
+  return launch_status("reduce_combine_kernel");
+}
+
+lmpb_status reduce_geometry(const int64_t* shape, int ndim, int axis, int64_t& outer, int64_t& R,
+                            int64_t& inner) {
+  LMPB_CHECK_ARG(ndim >= 1 && ndim <= LMPB_MAX_DIMS, "lmpb_reduce: bad ndim");
+  LMPB_CHECK_ARG(axis >= 0 && axis < ndim, "lmpb_reduce: axis out of range");
+  outer = 1;
+  inner = 1;
+  for (int i = 0; i < axis; ++i) outer *= shape[i];
+  for (int i = axis + 1; i < ndim; ++i) inner *= shape[i];
+  R = shape[axis];
+  return LMPB_OK;
+}
+
+// Runs a planned reduction with a caller-provided workspace of at least
+// plan.ws_bytes (may be null when ws_bytes == 0).
+lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64_t* shape,
+                                  int ndim, int axis, void* out, void* ws, size_t ws_bytes,
+                                  void* stream, bool allocate) {
+  LMPB_CHECK_ARG(valid_dtype(dtype), "lmpb_reduce: invalid dtype");
+  LMPB_CHECK_ARG(op >= LMPB_SUM && op <= LMPB_PROD, "lmpb_reduce: unknown op");
+  int64_t outer, R, inner;
+  lmpb_status s = reduce_geometry(shape, ndim, axis, outer, R, inner);
+  if (s != LMPB_OK) return s;
+  if (outer * inner == 0) return LMPB_OK;
+  LMPB_CHECK_ARG(in && out, "lmpb_reduce: null pointer");
+  cudaStream_t st = as_stream(stream);
+  LMPB_DISPATCH_DTYPE(dtype, T, {
+    ReducePlan p = plan_reduce<T>(in, out, outer, R, inner);
+    void* w = ws;
+    if (p.ws_bytes > 0) {
+      if (allocate) {
+        LMPB_CUDA_TRY(cudaMallocAsync(&w, p.ws_bytes, st));
+      } else {
+        LMPB_CHECK_ARG(w != nullptr && ws_bytes >= p.ws_bytes, "lmpb_reduce: workspace too small");
+      }
+    }
+    switch (op) {
+      case LMPB_SUM: s = run_reduce<LMPB_SUM, T>(p, (const T*)in, (T*)out, (T*)w, st); break;
+      case LMPB_MAX: s = run_reduce<LMPB_MAX, T>(p, (const T*)in, (T*)out, (T*)w, st); break;
+      case LMPB_MIN: s = run_reduce<LMPB_MIN, T>(p, (const T*)in, (T*)out, (T*)w, st); break;
+      default: s = run_reduce<LMPB_PROD, T>(p, (const T*)in, (T*)out, (T*)w, st); break;
+    }
+    if (allocate && p.ws_bytes > 0) {
+      cudaError_t e = cudaFreeAsync(w, st);
+      if (s == LMPB_OK && e != cudaSuccess)
+        return set_error(LMPB_ERR_CUDA, std::string("cudaFreeAsync: ") + cudaGetErrorString(e));
+    }
+    return s;
+  });
+  return set_error(LMPB_ERR_INVALID, "lmpb_reduce: invalid dtype");
+}
+
+}  // namespace lmpb
+
+extern "C" lmpb_status lmpb_reduce(int op, int dtype, const void* in, const int64_t* shape,
+                                   int ndim, int axis, void* out, void* stream) {
+  return lmpb::reduce_with_workspace(op, dtype, in, shape, ndim, axis, out, nullptr, 0, stream,
+                                     true);
+}
