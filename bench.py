@@ -1,0 +1,378 @@
+"""Benchmark of the Lamp3 B200 backend on the reference's headline workload.
+
+Default workload (the metric's fused elementwise case):
+    d = exp(a*a + b) * a - log(b + 1)   under capture_on, then d.backward()
+    a fp32 [8192, 8192] ~U[0,1), b fp32 [8192, 1] ~U[0,1), seeded.
+One step = the fused forward (d realized) + backward w.r.t. a and b (grads
+accumulate, as in the reference's timed loop).  Algorithmic bytes per step:
+    forward  = read a + read b + write d                 = 536,903,680 B
+    backward = read a + read b + RMW grad_a + RMW grad_b = 805,404,672 B
+value = algorithmic bytes of all ranks / max-over-ranks device time (GB/s).
+
+Multi-GPU (torchrun, one process per GPU): the chain is partitioned along the
+leading dim; each rank owns an [8192, 8192] row block of a [8192*N, 8192]
+problem (weak scaling).  No data-path collective: rows are independent.
+
+--impl reference runs the reference's own CPU implementation (its CPU core,
+compiled from its sources into oracle/_ref) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+ROWS, COLS = 8192, 8192
+FWD_BYTES = ROWS * COLS * 4 * 2 + ROWS * 4            # read a, write d, read b
+BWD_BYTES = ROWS * COLS * 4 * 3 + ROWS * 4 * 3        # read a, RMW grad_a, read b, RMW grad_b
+STEP_BYTES = FWD_BYTES + BWD_BYTES
+METRIC = "fused elementwise/reduction HBM GB/s (C2 broadcast chain fwd+bwd)"
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def inputs(rank: int):
+    rng = np.random.default_rng(1234 + rank)
+    a = rng.random((ROWS, COLS), dtype=np.float32)
+    b = rng.random((ROWS, 1), dtype=np.float32)
+    return a, b
+
+
+def chain(rsl, a, b):
+    return rsl.exp(a * a + b) * a - rsl.log(b + 1.0)
+
+
+def peak_hbm():
+    try:
+        with open(PEAKS) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.file = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self, t0=None, t1=None):
+        """Stops sampling; keeps the samples taken between wall times t0..t1."""
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.file.flush()
+        import datetime
+
+        rows = []
+        with open(self.file.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                try:
+                    ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    ts = None
+                if t0 is not None and ts is not None and not (t0 - 0.25 <= ts <= t1 + 0.25):
+                    continue
+                rows.append(parts[1:])
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_step(a, b):
+    """One C2 forward + backward on the reference's own CPU core (oracle/_ref)."""
+    from oracle import ref
+
+    A, B = ref.Var.of(a, True), ref.Var.of(b, True)
+    one = ref.Var.of(np.ones((1,), np.float32))
+    t0 = time.perf_counter()
+    d = ref.binary(1, ref.binary(2, ref.unary(1, ref.binary(0, ref.binary(2, A, A), B)), A),
+                   ref.unary(2, ref.binary(0, B, one)))
+    d.backward()
+    return time.perf_counter() - t0
+
+
+def cpu_kind():
+    from oracle import ref
+
+    return "reference" if ref.available() else "port"
+
+
+def cpu_port_step(a, b):
+    """The C restatement (oracle/port) of the same forward + closed-form backward."""
+    from oracle import port
+
+    t0 = time.perf_counter()
+    one = np.ones((1,), np.float32)
+    s = port.binary(2, a, a)
+    c = port.binary(0, s, b)
+    x = port.unary(1, c)
+    d = port.binary(1, port.binary(2, x, a), port.unary(2, port.binary(0, b, one)))
+    ga = port.binary(0, port.binary(2, x, port.binary(2, a, a)), x)
+    gb = port.reduce(0, port.binary(2, x, a), 1)
+    del d, ga, gb
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(a, b, budget_s=20.0):
+    kind = cpu_kind()
+    step = cpu_reference_step if kind == "reference" else cpu_port_step
+    step(a, b)  # warm-up (page faults)
+    times = []
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s and len(times) < 5:
+        times.append(step(a, b))
+    med = float(np.median(times))
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": STEP_BYTES / med / 1e9, "unit": "GB/s", "cores": cores if kind == "reference" else 1,
+            "kind": kind, "sample": f"{len(times)} full C2 steps (fwd+bwd, [8192,8192]) after 1 warm-up, median {med:.3f} s"}
+
+
+def run_reference_arm(args, rank, world):
+    """The reference's CPU implementation on the host cores.  Each step is a
+    row slice of the C2 workload (the same chain on [rows, 8192] with b
+    [rows, 1]) sized so that warm-up + K steps take about two minutes; the
+    metric is per byte, so it is independent of the slice height."""
+    if rank != 0:
+        return
+    a, b = inputs(0)
+    kind = cpu_kind()
+    step = cpu_reference_step if kind == "reference" else cpu_port_step
+    probe = 512
+    step(a[:probe], b[:probe])
+    t_probe = min(step(a[:probe], b[:probe]) for _ in range(2))
+    rows = int(probe * (120.0 / (args.steps + args.warmup)) / max(t_probe, 1e-6))
+    rows = max(8, min(ROWS, rows // 8 * 8))
+    sa, sb = np.ascontiguousarray(a[:rows]), np.ascontiguousarray(b[:rows])
+    for _ in range(args.warmup):
+        step(sa, sb)
+    times = [step(sa, sb) for _ in range(args.steps)]
+    total = float(np.sum(times))
+    bytes_per_step = STEP_BYTES * rows / ROWS
+    value = bytes_per_step * args.steps / total / 1e9
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded U[0,1))",
+        "config": {"workload": "C2 fused broadcast chain fwd+bwd", "a": [ROWS, COLS], "b": [ROWS, 1],
+                   "sample_rows": rows, "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{args.steps} steps of a [{rows}, {COLS}] row slice of C2 on the host CPU ({kind} CPU build)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_env()
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        pg = dist
+    import rushlite_b200 as rsl
+
+    rsl.cuda.set_device(local)
+    a_np, b_np = inputs(rank)
+    a = rsl.Variable(a_np, requires_grad=True, device=rsl.device.cuda)
+    b = rsl.Variable(b_np, requires_grad=True, device=rsl.device.cuda)
+
+    def step():
+        with rsl.capture_on():
+            d = chain(rsl, a, b)
+        d.realize()        # the fused forward writes d
+        d.backward()       # fused backward: grad_a, grad_b (row sums) in one pass
+        return d
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # timed region: device time via CUDA events on the launching stream (the
+    # legacy default stream, which the backend uses), per-phase events for the
+    # roofline of the dominant (backward) kernel
+    ev_start, ev_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    bwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    stream = torch.cuda.default_stream()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(1.0)  # let the sampler come up before the timed region
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    wall0 = time.time()
+    launches0 = rsl.cuda.kernel_launches()
+    ev_start.record(stream)
+    for i in range(args.steps):
+        with rsl.capture_on():
+            d = chain(rsl, a, b)
+        fwd_ev[i][0].record(stream)
+        d.realize()
+        fwd_ev[i][1].record(stream)
+        bwd_ev[i][0].record(stream)
+        d.backward()
+        bwd_ev[i][1].record(stream)
+    ev_end.record(stream)
+    torch.cuda.synchronize()
+    launches = rsl.cuda.kernel_launches() - launches0
+    wall1 = time.time()
+    if wall1 - wall0 < 1.0:
+        # the timed region was shorter than the sampling period: keep the same
+        # workload running for ~2 s more so the clock record has samples
+        t_end = time.time() + 2.0
+        while time.time() < t_end:
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
+        wall1 = time.time()
+        clk = clocks.stop(wall0, wall1)
+        clk["window"] = "timed region plus 2 s of the same steps (timed region shorter than the sampling period)"
+    else:
+        clk = clocks.stop(wall0, wall1)
+    if pg:
+        pg.barrier()
+    ms = ev_start.elapsed_time(ev_end)
+    fwd_ms = float(np.mean([s.elapsed_time(e) for s, e in fwd_ev]))
+    bwd_ms = float(np.mean([s.elapsed_time(e) for s, e in bwd_ev]))
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the public API with host buffers: pinned host inputs
+    # are uploaded, the step runs, d and both gradients come back to pinned
+    # host memory — every step, inside the timed region
+    pin_a = torch.empty((ROWS, COLS), dtype=torch.float32, pin_memory=True).numpy()
+    pin_b = torch.empty((ROWS, 1), dtype=torch.float32, pin_memory=True).numpy()
+    pin_d = torch.empty((ROWS, COLS), dtype=torch.float32, pin_memory=True).numpy()
+    pin_ga = torch.empty((ROWS, COLS), dtype=torch.float32, pin_memory=True).numpy()
+    pin_gb = torch.empty((ROWS, 1), dtype=torch.float32, pin_memory=True).numpy()
+    pin_a[...] = a_np
+    pin_b[...] = b_np
+
+    def e2e_step():
+        ea = rsl.Variable(pin_a, requires_grad=True, device=rsl.device.cuda)
+        eb = rsl.Variable(pin_b, requires_grad=True, device=rsl.device.cuda)
+        with rsl.capture_on():
+            d = chain(rsl, ea, eb)
+        d.numpy(out=pin_d)
+        d.backward()
+        ea.grad.numpy(out=pin_ga)
+        eb.grad.numpy(out=pin_gb)
+
+    e2e_step()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if pg:
+        t = torch.tensor([e2e_ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    if rank != 0:
+        if pg:
+            pg.destroy_process_group()
+        return
+
+    peak, peak_src = peak_hbm()
+    value = STEP_BYTES * args.steps * world / (ms / 1e3) / 1e9
+    achieved = BWD_BYTES / (bwd_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[0,1))",
+        "config": {"workload": "C2 fused broadcast chain fwd+bwd, capture_on", "a": [ROWS, COLS], "b": [ROWS, 1],
+                   "per_rank_rows": ROWS, "parallelism": f"row-partitioned x{world}",
+                   "l2": "inputs (268 MB) larger than the 126 MB L2; no flush needed",
+                   "algorithmic_bytes_per_step": STEP_BYTES},
+        "gpu_launches": int(launches),
+        "phases_ms": {"forward": fwd_ms, "backward": bwd_ms},
+        "roofline": {"bound": "hbm", "kernel": "fused backward (grad_a store + grad_b row-sum epilogue)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": None,
+                     "forward_achieved": FWD_BYTES / (fwd_ms / 1e3) / 1e9},
+        "clocks": clk,
+        "e2e": {"value": STEP_BYTES * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(pin_a.nbytes + pin_b.nbytes),
+                "d2h_bytes_per_step": int(pin_d.nbytes + pin_ga.nbytes + pin_gb.nbytes)},
+    }
+    if not args.no_cpu_baseline and world == 1:
+        try:
+            line["cpu_baseline"] = cpu_baseline(a_np, b_np)
+        except Exception as e:  # the reported baseline must never sink the GPU line
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    print(json.dumps(line), flush=True)
+    if pg:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

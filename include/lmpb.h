@@ -102,6 +102,9 @@ typedef enum { LMPB_H2D = 0, LMPB_D2H = 1, LMPB_D2D = 2, LMPB_H2H = 3 } lmpb_cop
 const char* lmpb_last_error(void);
 /* Library version string; also proves the library loaded. */
 const char* lmpb_version(void);
+/* Number of kernels this library has launched in the process (all devices).
+ * No counterpart in the reference; used to count launches in benchmarks. */
+uint64_t lmpb_kernel_launches(void);
 
 /* ------------------------------------------------------------ shapes */
 

@@ -38,7 +38,7 @@ STATUS = {0: "OK", 1: "INVALID", 2: "CUDA", 3: "UNSUPPORTED", 4: "COMPILE", 5: "
 
 # every symbol include/lmpb.h declares
 EXPORTS = [
-    "lmpb_last_error", "lmpb_version", "lmpb_broadcast_shape", "lmpb_binary", "lmpb_unary",
+    "lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_broadcast_shape", "lmpb_binary", "lmpb_unary",
     "lmpb_reduce", "lmpb_matmul", "lmpb_gemm_f32", "lmpb_transpose", "lmpb_malloc", "lmpb_free",
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
     "lmpb_fused_release", "lmpb_fused_source",
@@ -77,6 +77,7 @@ def lib() -> C.CDLL:
         vp, i64, i32, d, P64 = C.c_void_p, C.c_int64, C.c_int, C.c_double, C.POINTER(C.c_int64)
         L.lmpb_last_error.restype = C.c_char_p
         L.lmpb_version.restype = C.c_char_p
+        L.lmpb_kernel_launches.restype = C.c_uint64
         L.lmpb_broadcast_shape.argtypes = [P64, i32, P64, i32, P64, C.POINTER(C.c_int)]
         L.lmpb_binary.argtypes = [i32, i32, vp, i32, P64, i32, vp, i32, P64, i32, vp, d, d, vp]
         L.lmpb_unary.argtypes = [i32, i32, vp, vp, i64, d, d, vp]
@@ -96,7 +97,7 @@ def lib() -> C.CDLL:
         L.lmpb_fused_source.argtypes = [vp]
         L.lmpb_fused_source.restype = C.c_char_p
         for name in EXPORTS:
-            if name not in ("lmpb_last_error", "lmpb_version", "lmpb_fused_source"):
+            if name not in ("lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_fused_source"):
                 getattr(L, name).restype = C.c_int
         _lib = L
     return _lib
@@ -194,3 +195,7 @@ class Fused:
         if getattr(self, "h", None) and _lib is not None:
             _lib.lmpb_fused_release(self.h)
             self.h = None
+
+
+def kernel_launches() -> int:
+    return int(lib().lmpb_kernel_launches())

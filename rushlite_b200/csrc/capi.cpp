@@ -2,6 +2,7 @@
 // queries.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -12,7 +13,10 @@ namespace lmpb {
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
 }
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 lmpb_status set_error(lmpb_status st, const std::string& msg) {
   g_last_error = msg;
@@ -20,6 +24,7 @@ lmpb_status set_error(lmpb_status st, const std::string& msg) {
 }
 
 lmpb_status launch_status(const char* what) {
+  count_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return set_error(LMPB_ERR_CUDA, std::string(what) + " launch failed: " + cudaGetErrorString(e));
@@ -54,6 +59,8 @@ int sm_count() {
 extern "C" const char* lmpb_last_error(void) { return lmpb::g_last_error.c_str(); }
 
 extern "C" const char* lmpb_version(void) { return "lmpb 0.1 sm_100a"; }
+
+extern "C" uint64_t lmpb_kernel_launches(void) { return lmpb::g_launches.load(); }
 
 extern "C" lmpb_status lmpb_broadcast_shape(const int64_t* a_shape, int a_ndim,
                                             const int64_t* b_shape, int b_ndim,

@@ -47,6 +47,7 @@ lmpb_status set_error(lmpb_status st, const std::string& msg);
 bool valid_dtype(int dt);
 size_t dtype_size(int dt);
 int sm_count();
+void count_launch();
 }  // namespace lmpb
 
 using lmpb::set_error;
@@ -715,10 +716,13 @@ lmpb_status cu_err(CUresult r, const char* what) {
 }
 
 lmpb_status get_functions(lmpb_fused_s& h, std::array<CUfunction, 3>& fns) {
-  cudaFree(nullptr);  // make sure the runtime made the primary context current
   if (!drv().ok) return set_error(LMPB_ERR_CUDA, "fused: CUDA driver entry points unavailable");
   CUcontext ctx = nullptr;
   CUresult r = drv().ctxGetCurrent(&ctx);
+  if (r == CUDA_SUCCESS && ctx == nullptr) {
+    cudaFree(nullptr);  // first runtime call on this thread: make the primary context current
+    r = drv().ctxGetCurrent(&ctx);
+  }
   if (r != CUDA_SUCCESS || ctx == nullptr) return set_error(LMPB_ERR_CUDA, "fused: no current CUDA context");
   std::lock_guard<std::mutex> lk(h.mu);
   auto it = h.fn.find(ctx);
@@ -858,6 +862,7 @@ extern "C" lmpb_status lmpb_fused_launch(lmpb_fused h, const void* const* leaf_p
                     CU_LAUNCH_PARAM_END};
   (void)args;
   CUresult r = drv().launchKernel(f, gx, gy, 1, kThreads, 1, 1, 0, reinterpret_cast<CUstream>(stream), nullptr, config);
+  lmpb::count_launch();
   if (r != CUDA_SUCCESS) {
     if (ws) cudaFreeAsync(ws, cst);
     return cu_err(r, "cuLaunchKernel(fused)");
@@ -866,6 +871,7 @@ extern "C" lmpb_status lmpb_fused_launch(lmpb_fused h, const void* const* leaf_p
     int64_t b = (p.size[1] + kThreads - 1) / kThreads;
     unsigned g2 = (unsigned)std::max<int64_t>(1, std::min(b, cap));
     r = drv().launchKernel(fns[2], g2, 1, 1, kThreads, 1, 1, 0, reinterpret_cast<CUstream>(stream), nullptr, config);
+    lmpb::count_launch();
     if (r != CUDA_SUCCESS) {
       cudaFreeAsync(ws, cst);
       return cu_err(r, "cuLaunchKernel(fused combine)");

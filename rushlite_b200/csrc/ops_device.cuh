@@ -52,6 +52,30 @@ template <> __device__ __forceinline__ double r_add<double>(double a, double b) 
 template <> __device__ __forceinline__ double r_sub<double>(double a, double b) { return __dsub_rn(a, b); }
 template <> __device__ __forceinline__ double r_mul<double>(double a, double b) { return __dmul_rn(a, b); }
 
+// Integral pow.  The reference computes std::pow in double and truncates
+// (PowFunctor, kernels.hpp:36-41); glibc's pow is exact whenever the result is
+// an exactly representable double, CUDA's device pow is not (3^1 can come out
+// as 2.9999999999999996 and truncate to 2).  For an integral exponent >= 0 the
+// power is built by binary exponentiation in double, exact up to 2^53; a
+// negative exponent gives |result| < 1 (truncates to 0) except for bases 1/-1.
+template <typename T>
+__device__ __forceinline__ T int_pow(T a, T b) {
+  long long e = static_cast<long long>(b);
+  if (e < 0) {
+    if (a == T(1)) return T(1);
+    if (a == static_cast<T>(-1)) return (e & 1) ? static_cast<T>(-1) : T(1);
+    if (a == T(0)) return static_cast<T>(1.0 / 0.0);
+    return T(0);
+  }
+  double base = static_cast<double>(a), r = 1.0;
+  while (e) {
+    if (e & 1) r *= base;
+    e >>= 1;
+    if (e) base *= base;
+  }
+  return static_cast<T>(r);
+}
+
 template <int OP, typename T>
 __device__ __forceinline__ T binary_apply(T a, T b, T lo, T hi) {
   if constexpr (OP == B_ADD) return static_cast<T>(r_add(a, b));
@@ -61,8 +85,10 @@ __device__ __forceinline__ T binary_apply(T a, T b, T lo, T hi) {
     if constexpr (is_fp<T>::value) return a / b;
     else return b == T(0) ? T(0) : static_cast<T>(a / b);  // the CPU traps on x/0; a GPU must not
   }
-  else if constexpr (OP == B_POW)
-    return static_cast<T>(m_pow(static_cast<math_t<T>>(a), static_cast<math_t<T>>(b)));
+  else if constexpr (OP == B_POW) {
+    if constexpr (is_fp<T>::value) return m_pow(a, b);
+    else return int_pow<T>(a, b);
+  }
   else if constexpr (OP == B_EQ) return static_cast<T>(a == b);
   else if constexpr (OP == B_NE) return static_cast<T>(a != b);
   else if constexpr (OP == B_GE) return static_cast<T>(a >= b);
