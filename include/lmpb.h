@@ -171,6 +171,12 @@ lmpb_status lmpb_matmul(int out_dtype, const void* A, int a_dtype, const void* B
 lmpb_status lmpb_gemm_f32(int trans_a, int trans_b, const float* A, const float* B, float* C,
                           int64_t m, int64_t n, int64_t k, float beta, void* stream);
 
+/* LMPB_ERR_TIMEOUT if a bounded device wait inside a kernel expired since
+ * the last call (the kernel then stopped early and its output is invalid),
+ * else LMPB_OK.  Synchronises the current device.  No counterpart in the
+ * reference, whose kernels have no device-side waits. */
+lmpb_status lmpb_device_error(void);
+
 /* out[n,m] = in[m,n]ᵀ (transpose_cuda, csrc/src/tensor/cuda/kernels.cu:66-81). */
 lmpb_status lmpb_transpose(int dtype, const void* in, void* out, int64_t m, int64_t n,
                            void* stream);

@@ -41,7 +41,7 @@ EXPORTS = [
     "lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_broadcast_shape", "lmpb_binary", "lmpb_unary",
     "lmpb_reduce", "lmpb_matmul", "lmpb_gemm_f32", "lmpb_transpose", "lmpb_malloc", "lmpb_free",
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
-    "lmpb_fused_release", "lmpb_fused_source",
+    "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error",
 ]
 
 
@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
         L.lmpb_matmul.argtypes = [i32, vp, i32, vp, i32, vp, i64, i64, i64, vp]
         L.lmpb_gemm_f32.argtypes = [i32, i32, vp, vp, vp, i64, i64, i64, C.c_float, vp]
         L.lmpb_transpose.argtypes = [i32, vp, vp, i64, i64, vp]
+        L.lmpb_device_error.argtypes = []
         L.lmpb_malloc.argtypes = [C.POINTER(vp), C.c_size_t, vp]
         L.lmpb_free.argtypes = [vp, vp]
         L.lmpb_fill.argtypes = [i32, vp, i64, d, vp]
@@ -199,3 +200,8 @@ class Fused:
 
 def kernel_launches() -> int:
     return int(lib().lmpb_kernel_launches())
+
+
+def device_error() -> None:
+    """Raises if a bounded device wait expired since the last call."""
+    check(lib().lmpb_device_error())

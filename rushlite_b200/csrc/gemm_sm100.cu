@@ -1,4 +1,39 @@
-// fp32 GEMM entry used by lmpb_matmul / lmpb_gemm_f32.
+// fp32 GEMM on the B200 tensor cores: 3xTF32 with tcgen05, TMEM and TMA.
+//
+//   C[m,n] = op(A)[m,k] · op(B)[k,n] (+ C when beta = 1), fp32 in and out.
+//
+// fp32 accuracy is kept by splitting every operand element x into
+// hi = tf32(x) and lo = tf32(x - hi) (round to nearest) and accumulating
+// hi·hi + hi·lo + lo·hi in fp32 in TMEM; the dropped lo·lo term and the tf32
+// rounding of lo are O(2^-22) relative, below fp32 accumulation error.
+//
+// 1. A split pass writes hi and lo planes of both operands, K-major (rows of
+//    K contiguous fp32, K padded to the k-block), transposing op(A) / op(B)
+//    on the way when the caller's layout is not K-major.  It reads each input
+//    element once and writes 8 bytes; for 4096^3 that is ~1.5% of the GEMM.
+// 2. The GEMM kernel: one CTA per 128 x BN output tile, 6 warps:
+//      warp 0     TMA producer (one elected thread): 4 tiles per k-block
+//                 (A hi/lo, B hi/lo) into a STAGES-deep shared-memory ring,
+//                 128-byte swizzled, completion on an mbarrier;
+//      warp 1     owns the TMEM accumulator (128 lanes x BN fp32 columns) and
+//                 issues the tcgen05.mma.kind::tf32 instructions (one thread),
+//                 3 products x BK/8 MMAs per k-block, then tcgen05.commit
+//                 frees the stage;
+//      warps 2-5  epilogue: tcgen05.ld 32x32b from TMEM (each warp reads the
+//                 32 lanes its rank in the warpgroup may access), optional
+//                 + C, 16-byte stores.
+//    Every mbarrier wait is bounded (clock64); on expiry the kernel records
+//    an error code in a device word, stops issuing, frees TMEM and returns.
+//    No cluster launch and no multicast: each CTA loads its own tiles.
+// Shapes that TMA cannot describe or that are too small for a 128-row tile
+// use the SIMT kernel (gemm_simt.cu).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace lmpb {
@@ -6,9 +41,394 @@ namespace lmpb {
 lmpb_status gemm_f32_simt(int ta, int tb, const float* A, const float* B, float* C, int64_t m,
                           int64_t n, int64_t k, float beta, cudaStream_t st);
 
-lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float* B, float* C,
-                           int64_t m, int64_t n, int64_t k, float beta, cudaStream_t st) {
-  return gemm_f32_simt(trans_a, trans_b, A, B, C, m, n, k, beta, st);
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 32;      // 32 fp32 = 128 bytes per row = one 128B swizzle atom
+constexpr int STAGES = 2;
+constexpr int kThreads = 192;
+constexpr int A_TILE = BM * BK * 4;  // 16 KB
+constexpr int B_TILE = BN * BK * 4;  // 32 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+// Device error word: 0 = ok, else the code of the first bounded wait that expired.
+__device__ unsigned int g_gemm_error = 0;
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false (and the error word set to `code`) after kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned code) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(&g_gemm_error, 0u, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// K-major, 128B-swizzled tile: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFF) >> 4);  // start address
+  d |= (uint64_t)1 << 16;                  // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;        // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                  // SWIZZLE_128B
+  return d;
+}
+
+// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=BN.
+__host__ __device__ constexpr uint32_t instr_desc() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------ split pass
+
+// Round to the nearest tf32 value (10 explicit mantissa bits), ties to even.
+__device__ __forceinline__ float tf32_rne(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) != 0x7F800000u) {  // finite
+    u += 0x0FFFu + ((u >> 13) & 1u);
+    u &= 0xFFFFE000u;
+  }
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ void split(float x, float& hi, float& lo) {
+  hi = tf32_rne(x);
+  lo = tf32_rne(__fsub_rn(x, hi));
+}
+
+// src is [rows, K] row-major: hi/lo [rows, Kp] with zero padding.
+__global__ void __launch_bounds__(256)
+    split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
+                        float* __restrict__ hi, float* __restrict__ lo) {
+  const int64_t n = rows * Kp;
+  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+    const int64_t r = i / Kp, c = i - r * Kp;
+    float h = 0.f, l = 0.f;
+    if (c < K) split(src[r * K + c], h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// src is [K, rows] row-major (the operand transposed): hi/lo [rows, Kp].
+__global__ void __launch_bounds__(256)
+    split_transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
+                           float* __restrict__ hi, float* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.y * 32, r0 = (int64_t)blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t k = k0 + j, r = r0 + tx;
+    tile[j][tx] = (k < K && r < rows) ? src[k * rows + r] : 0.f;
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int64_t r = r0 + j, k = k0 + tx;
+    if (r < rows && k < Kp) {
+      float h, l;
+      split(tile[tx][j], h, l);
+      hi[r * Kp + k] = h;
+      lo[r * Kp + k] = l;
+    }
+  }
+}
+
+// ------------------------------------------------------------ GEMM kernel
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
+                       const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
+                       float* __restrict__ C, int M, int N, int num_kb, int beta) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accum = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // tile rasterisation: groups of 8 row-tiles share B panels in L2
+  const int tiles_n = gridDim.x, tiles_m = gridDim.y;
+  const int tid = blockIdx.y * tiles_n + blockIdx.x;
+  const int group = 8;
+  const int g = tid / (group * tiles_n);
+  const int first_m = g * group;
+  const int gsize = min(tiles_m - first_m, group);
+  const int tm = first_m + (tid % (group * tiles_n)) % gsize;
+  const int tn = (tid % (group * tiles_n)) / gsize;
+  const int m0 = tm * BM, n0 = tn * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    mbar_init(smem_u32(accum), 1);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAh)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAl)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBh)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBl)) : "memory");
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t phase = (kb / STAGES) & 1;
+      if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, 1)) break;
+      uint8_t* st = smem + s * STAGE_BYTES;
+      const uint32_t bar = smem_u32(&full[s]);
+      mbar_expect_tx(bar, STAGE_BYTES);
+      tma_load_2d(smem_u32(st), &tAh, kb * BK, m0, bar);
+      tma_load_2d(smem_u32(st + A_TILE), &tAl, kb * BK, m0, bar);
+      tma_load_2d(smem_u32(st + 2 * A_TILE), &tBh, kb * BK, n0, bar);
+      tma_load_2d(smem_u32(st + 2 * A_TILE + B_TILE), &tBl, kb * BK, n0, bar);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer
+    constexpr uint32_t idesc = instr_desc();
+    bool ok = true;
+    for (int kb = 0; kb < num_kb && ok; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t phase = (kb / STAGES) & 1;
+      if (!mbar_wait(smem_u32(&full[s]), phase, 2)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+      const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_TILE);
+      const uint64_t dBh = smem_desc(base + 2 * A_TILE), dBl = smem_desc(base + 2 * A_TILE + B_TILE);
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
+        const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+        mma_tf32(tmem, dAl + off, dBh + off, idesc, first);  // small terms first
+        mma_tf32(tmem, dAh + off, dBl + off, idesc, 1u);
+        mma_tf32(tmem, dAh + off, dBh + off, idesc, 1u);
+      }
+      mma_commit(smem_u32(&empty[s]));
+    }
+    mma_commit(smem_u32(accum));
+  } else if (warp >= 2) {
+    // ---- epilogue: TMEM -> registers -> global
+    const bool ok = mbar_wait(smem_u32(accum), 0, 3);
+    tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = m0 + q * 32 + lane;
+    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+    const bool vec = (N & 3) == 0;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(taddr + c, r);
+      if (!ok || row >= M) continue;
+      float* crow = C + (int64_t)row * N + n0 + c;
+      const int ncols = min(16, N - (n0 + c));
+      if (ncols <= 0) continue;
+      if (vec && ncols == 16) {
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                 __uint_as_float(r[j + 3]));
+          if (beta) {
+            const float4 o = *reinterpret_cast<const float4*>(crow + j);
+            v.x = __fadd_rn(o.x, v.x);
+            v.y = __fadd_rn(o.y, v.y);
+            v.z = __fadd_rn(o.z, v.z);
+            v.w = __fadd_rn(o.w, v.w);
+          }
+          *reinterpret_cast<float4*>(crow + j) = v;
+        }
+      } else {
+        for (int j = 0; j < ncols; ++j) {
+          float v = __uint_as_float(r[j]);
+          if (beta) v = __fadd_rn(crow[j], v);
+          crow[j] = v;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ host side
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiled) nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// Tensor map over a [rows, Kp] fp32 plane, box = box_rows x BK, 128B swizzle.
+lmpb_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t Kp, int box_rows) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return set_error(LMPB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(LMPB_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return LMPB_OK;
+}
+
+lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K, int64_t Kp, float* hi,
+                          float* lo, cudaStream_t st) {
+  if (kmajor) {
+    const int64_t n = rows * Kp;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
+    split_kmajor_kernel<<<(int)blocks, 256, 0, st>>>(src, rows, K, Kp, hi, lo);
+  } else {
+    if ((Kp + 31) / 32 > 65535) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
+    dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((Kp + 31) / 32));
+    split_transpose_kernel<<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo);
+  }
+  return launch_status("gemm split pass");
+}
+
+}  // namespace
+
+// Tensor-core path for problems that fill 128-row tiles; SIMT otherwise.
+lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float* B, float* C, int64_t m,
+                           int64_t n, int64_t k, float beta, cudaStream_t st) {
+  const bool small = m < 64 || n < 64 || k < 32 || (double)m * n * k < 2.0e6;
+  if (small || m > (1ll << 30) || n > (1ll << 30) || getenv("LMPB_GEMM_SIMT"))
+    return gemm_f32_simt(trans_a, trans_b, A, B, C, m, n, k, beta, st);
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(attr_err));
+  const int64_t Kp = (k + BK - 1) / BK * BK;
+  const size_t plane_a = (size_t)m * Kp * 4, plane_b = (size_t)n * Kp * 4;
+  void* ws = nullptr;
+  LMPB_CUDA_TRY(cudaMallocAsync(&ws, 2 * plane_a + 2 * plane_b, st));
+  float* Ah = static_cast<float*>(ws);
+  float* Al = reinterpret_cast<float*>(static_cast<char*>(ws) + plane_a);
+  float* Bh = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * plane_a);
+  float* Bl = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * plane_a + plane_b);
+  // op(A) is [m,k]: K-major as stored unless transposed; the MMA's B operand
+  // is op(B)^T = [n,k]: K-major as stored only when trans_b.
+  lmpb_status s = split_operand(A, !trans_a, m, k, Kp, Ah, Al, st);
+  if (s == LMPB_OK) s = split_operand(B, trans_b != 0, n, k, Kp, Bh, Bl, st);
+  CUtensorMap mAh, mAl, mBh, mBl;
+  if (s == LMPB_OK) s = make_map(&mAh, Ah, m, Kp, BM);
+  if (s == LMPB_OK) s = make_map(&mAl, Al, m, Kp, BM);
+  if (s == LMPB_OK) s = make_map(&mBh, Bh, n, Kp, BN);
+  if (s == LMPB_OK) s = make_map(&mBl, Bl, n, Kp, BN);
+  if (s == LMPB_OK) {
+    dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
+    if (grid.y > 65535) {
+      s = set_error(LMPB_ERR_UNSUPPORTED, "gemm: m too large");
+    } else {
+      gemm_3xtf32_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, C, (int)m, (int)n,
+                                                             (int)(Kp / BK), beta != 0.f ? 1 : 0);
+      s = launch_status("gemm_3xtf32_kernel");
+    }
+  }
+  cudaError_t e = cudaFreeAsync(ws, st);
+  if (s == LMPB_OK && e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("cudaFreeAsync: ") + cudaGetErrorString(e));
+  return s;
+}
+
+// Reads and clears the device error word of the tensor-core GEMM (0 = none).
+unsigned int gemm_take_error() {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof v) != cudaSuccess) return 0xFFFFFFFFu;
+  if (v) cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof zero);
+  return v;
 }
 
 }  // namespace lmpb

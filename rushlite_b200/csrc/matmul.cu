@@ -9,6 +9,7 @@ namespace lmpb {
 // Declared in gemm_sm100.cu.
 lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float* B, float* C,
                            int64_t m, int64_t n, int64_t k, float beta, cudaStream_t st);
+unsigned int gemm_take_error();
 
 namespace {
 
@@ -71,4 +72,11 @@ extern "C" lmpb_status lmpb_gemm_f32(int trans_a, int trans_b, const float* A, c
   LMPB_CHECK_ARG(C != nullptr && (k == 0 || (A && B)), "lmpb_gemm_f32: null pointer");
   if (k == 0) return beta == 0.f ? lmpb_fill(LMPB_FLOAT32, C, m * n, 0.0, stream) : LMPB_OK;
   return gemm_f32_sm100(trans_a, trans_b, A, B, C, m, n, k, beta, as_stream(stream));
+}
+
+extern "C" lmpb_status lmpb_device_error(void) {
+  LMPB_CUDA_TRY(cudaDeviceSynchronize());
+  const unsigned int e = gemm_take_error();
+  if (e == 0) return LMPB_OK;
+  return set_error(LMPB_ERR_TIMEOUT, "tensor-core GEMM: a bounded wait expired (code " + std::to_string(e) + ")");
 }
