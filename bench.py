@@ -251,8 +251,12 @@ def main():
     # legacy default stream, which the backend uses), per-phase events for the
     # roofline of the dominant (backward) kernel
     ev_start, ev_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    fwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    bwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    # phase events on every PHASE_EVERY-th step only: recording events between
+    # the kernels of every step perturbs the timeline measurably
+    PHASE_EVERY = 8
+    n_ph = (args.steps + PHASE_EVERY - 1) // PHASE_EVERY
+    fwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ph)]
+    bwd_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_ph)]
     stream = torch.cuda.default_stream()
     clocks = Clocks(local)
     clocks.start()
@@ -266,12 +270,17 @@ def main():
     for i in range(args.steps):
         with rsl.capture_on():
             d = chain(rsl, a, b)
-        fwd_ev[i][0].record(stream)
-        d.realize()
-        fwd_ev[i][1].record(stream)
-        bwd_ev[i][0].record(stream)
-        d.backward()
-        bwd_ev[i][1].record(stream)
+        if i % PHASE_EVERY == 0:
+            j = i // PHASE_EVERY
+            fwd_ev[j][0].record(stream)
+            d.realize()
+            fwd_ev[j][1].record(stream)
+            bwd_ev[j][0].record(stream)
+            d.backward()
+            bwd_ev[j][1].record(stream)
+        else:
+            d.realize()
+            d.backward()
     ev_end.record(stream)
     torch.cuda.synchronize()
     launches = rsl.cuda.kernel_launches() - launches0

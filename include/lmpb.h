@@ -220,7 +220,8 @@ lmpb_status lmpb_add_inplace(int dtype, void* dst, const void* src, int64_t n, v
  * mode: STORE writes the full iteration space, ACCUM adds into an existing
  * full-size buffer (add_inplace fused in), REDUCE_SUM / REDUCE_SUM_ACCUM sum
  * the node over the axes where out_shape is 1 (the sum_broadcast_axis of
- * csrc/src/autograd/utils/grad_utils.cpp:10-36) and store or accumulate. */
+ * csrc/src/autograd/utils/grad_utils.cpp:10-36), add the optional addend
+ * node, and store or accumulate. */
 typedef enum {
   LMPB_FN_LEAF = 0,   /* reads leaf slot `a` */
   LMPB_FN_CONST = 1,  /* the constant p0 */
@@ -251,9 +252,13 @@ typedef enum {
 
 typedef struct {
   int32_t node;
-  int32_t mode;  /* lmpb_fout_mode */
-  int32_t dtype; /* dtype of the output buffer */
+  int32_t mode;    /* lmpb_fout_mode */
+  int32_t dtype;   /* dtype of the output buffer */
+  int32_t addend;  /* REDUCE_* only: node added to the sum (-1: none); it must
+                      not vary along the reduced axes, e.g. the elementwise
+                      terms of a gradient that also receives a broadcast sum */
   int32_t ndim;
+  int32_t reserved;
   int64_t shape[LMPB_MAX_DIMS]; /* == iter shape, or with 1s on reduced axes */
 } lmpb_fout;
 

@@ -61,8 +61,8 @@ class FLeaf(C.Structure):
 
 
 class FOut(C.Structure):
-    _fields_ = [("node", C.c_int32), ("mode", C.c_int32), ("dtype", C.c_int32),
-                ("ndim", C.c_int32), ("shape", C.c_int64 * MAX_DIMS)]
+    _fields_ = [("node", C.c_int32), ("mode", C.c_int32), ("dtype", C.c_int32), ("addend", C.c_int32),
+                ("ndim", C.c_int32), ("reserved", C.c_int32), ("shape", C.c_int64 * MAX_DIMS)]
 
 
 _lib = None
@@ -174,8 +174,10 @@ class Fused:
             for k, s in enumerate(shape):
                 la[i].shape[k] = s
         oa = (FOut * len(outs))()
-        for j, (node, mode, dt, shape) in enumerate(outs):
+        for j, out in enumerate(outs):
+            node, mode, dt, shape = out[:4]
             oa[j].node, oa[j].mode, oa[j].dtype, oa[j].ndim = node, mode, dt, len(shape)
+            oa[j].addend = out[4] if len(out) > 4 else -1
             for k, s in enumerate(shape):
                 oa[j].shape[k] = s
         h = C.c_void_p()

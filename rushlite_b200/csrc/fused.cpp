@@ -446,9 +446,11 @@ struct Gen {
       const std::string O = "O" + std::to_string(j);
       // output offset along P (group 0)
       const std::string oo = p.out_stride[j][0] == 0 ? "0" : "row * " + std::to_string(p.out_stride[j][0]) + "u";
+      const int ad = h.outs[j].addend;
+      const std::string val = ad >= 0 ? "lmpb_dev::r_add<" + OT + ">(static_cast<" + OT + ">(v" + std::to_string(ad) + "), " + a + ")" : a;
       std::string wr = p.out_mode[j] == LMPB_OUT_REDUCE_SUM_ACCUM
-                           ? O + "[" + oo + "] = lmpb_dev::r_add<" + OT + ">(" + O + "[" + oo + "], " + a + ");"
-                           : O + "[" + oo + "] = " + a + ";";
+                           ? O + "[" + oo + "] = lmpb_dev::r_add<" + OT + ">(" + O + "[" + oo + "], " + val + ");"
+                           : O + "[" + oo + "] = " + val + ";";
       os << "    " << a << " = warp_sum(" << a << ");\n";
       if (W) {
         os << "    if (lane == 0) " << wr << "\n";
@@ -499,16 +501,21 @@ struct Gen {
       if (p.out_mode[j] < LMPB_OUT_REDUCE_SUM) continue;
       const std::string OT = tname(h.outs[j].dtype);
       const std::string O = "O" + std::to_string(j);
+      const int ad = h.outs[j].addend;
+      const std::string acc = "acc" + std::to_string(j) + "[j]";
+      const std::string val = ad >= 0 ? "lmpb_dev::r_add<" + OT + ">(static_cast<" + OT + ">(" + ref(ad, true) + "), " + acc + ")" : acc;
       if (p.S > 1) {
+        // chunk 0 carries the addend; the combine kernel sums chunks in order
         os << "  { " << OT << "* W = reinterpret_cast<" << OT << "*>(static_cast<char*>(prm.ws) + " << h.ws_offset[j] << "ull);\n"
-           << "    #pragma unroll\n    for (int j = 0; j < " << vec << "; ++j) W[blockIdx.y * " << Q << "ull + q + j] = acc" << j << "[j]; }\n";
+           << "    #pragma unroll\n    for (int j = 0; j < " << vec << "; ++j) W[blockIdx.y * " << Q << "ull + q + j] = "
+           << (ad >= 0 ? "blockIdx.y == 0 ? " + val + " : " + acc : acc) << "; }\n";
       } else {
         const std::string oo = "q + j";
         os << "  #pragma unroll\n  for (int j = 0; j < " << vec << "; ++j) ";
         if (p.out_mode[j] == LMPB_OUT_REDUCE_SUM_ACCUM)
-          os << O << "[" << oo << "] = lmpb_dev::r_add<" << OT << ">(" << O << "[" << oo << "], acc" << j << "[j]);\n";
+          os << O << "[" << oo << "] = lmpb_dev::r_add<" << OT << ">(" << O << "[" << oo << "], " << val << ");\n";
         else
-          os << O << "[" << oo << "] = acc" << j << "[j];\n";
+          os << O << "[" << oo << "] = " << val << ";\n";
       }
     }
     os << "}\n";
@@ -794,6 +801,19 @@ extern "C" lmpb_status lmpb_fused_build(const lmpb_fnode* nodes, int n_nodes, co
   h->outs.assign(outs, outs + n_outs);
   lmpb_status st = make_plan(*h, iter_shape, iter_ndim);
   if (st != LMPB_OK) return st;
+  {
+    Gen g(*h, 1);
+    for (int j = 0; j < n_outs; ++j) {
+      const int ad = outs[j].addend;
+      if (ad < 0) continue;
+      const int mode = h->plan.out_mode[j];
+      if (ad >= n_nodes || mode < LMPB_OUT_REDUCE_SUM)
+        return set_error(LMPB_ERR_INVALID, "fused: an addend needs a reduce output");
+      for (int gi = 0; gi < h->plan.G; ++gi)
+        if (h->plan.out_stride[j][gi] == 0 && h->plan.size[gi] > 1 && g.varies[ad][gi])
+          return set_error(LMPB_ERR_INVALID, "fused: the addend varies along a reduced axis");
+    }
+  }
   h->ws_offset.assign(n_outs, 0);
   if (h->plan.pattern == kColReduce && h->plan.S > 1) {
     size_t off = 0;

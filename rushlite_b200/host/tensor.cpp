@@ -380,10 +380,58 @@ struct ProgramBuilder {
     return add_node(n);
   }
 
+  // True when no realized leaf under `t` has extent > 1 on the axes that a
+  // sum from shape `full` down to shape `target` reduces.
+  static bool invariant_along(TensorImpl* t, const std::vector<size_t>& full, const std::vector<size_t>& target,
+                              std::unordered_set<TensorImpl*>& seen) {
+    if (!seen.insert(t).second) return true;
+    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum) {
+      const size_t nd = full.size();
+      for (size_t k = 0; k < nd; ++k) {
+        const size_t d = nd - 1 - k;
+        const bool reduced = full[d] != 1 && (k >= target.size() || target[target.size() - 1 - k] == 1);
+        if (!reduced) continue;
+        if (k < t->shape.size() && t->shape[t->shape.size() - 1 - k] != 1) return false;
+      }
+      return true;
+    }
+    for (const auto& in : t->lazy->inputs)
+      if (!invariant_along(in.get(), full, target, seen)) return false;
+    return true;
+  }
+
   int visit(TensorImpl* t) {
     auto it = memo.find(t);
     if (it != memo.end()) return it->second;
     int id;
+    if (t->lazy && t->lazy->kind == LazyNode::kReduceSum && nodes.size() <= budget) {
+      // A sum over axes its input does not vary along is that value times the
+      // number of summed elements: no reduction kernel needed.
+      TensorImpl* x = t->lazy->inputs[0].get();
+      std::unordered_set<TensorImpl*> seen;
+      if (invariant_along(x, x->shape, t->shape, seen)) {
+        size_t count = 1;
+        const size_t nd = x->shape.size();
+        for (size_t k = 0; k < nd; ++k) {
+          const size_t d = nd - 1 - k;
+          if (x->shape[d] != 1 && (k >= t->shape.size() || t->shape[t->shape.size() - 1 - k] == 1)) count *= x->shape[d];
+        }
+        lmpb_fnode c{};
+        c.kind = LMPB_FN_CONST;
+        c.dtype = (int)t->dtype;
+        c.p0 = (double)count;
+        const int cn = add_node(c);
+        lmpb_fnode m{};
+        m.kind = LMPB_FN_BINARY;
+        m.sub = LMPB_MUL;
+        m.dtype = (int)t->dtype;
+        m.a = visit(x);
+        m.b = cn;
+        id = add_node(m);
+        memo[t] = id;
+        return id;
+      }
+    }
     if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || nodes.size() > budget) {
       id = leaf(t);  // realizes barriers / oversize sub-graphs first
     } else {
@@ -410,10 +458,26 @@ struct ProgramBuilder {
     return id;
   }
 
-  void output(int node, int mode, DataType dt, const std::vector<size_t>& shape, void* ptr) {
+  // Left-to-right ADD chain over `terms` in dtype dt.
+  int chain(const std::vector<ImplPtr>& terms, DataType dt) {
+    int node = visit(terms[0].get());
+    for (size_t i = 1; i < terms.size(); ++i) {
+      lmpb_fnode n{};
+      n.kind = LMPB_FN_BINARY;
+      n.sub = LMPB_ADD;
+      n.dtype = (int)dt;
+      n.a = node;
+      n.b = visit(terms[i].get());
+      node = add_node(n);
+    }
+    return node;
+  }
+
+  void output(int node, int mode, DataType dt, const std::vector<size_t>& shape, void* ptr, int addend = -1) {
     lmpb_fout o{};
     o.node = node;
     o.mode = mode;
+    o.addend = addend;
     o.dtype = (int)dt;
     o.ndim = (int)shape.size();
     for (size_t i = 0; i < shape.size(); ++i) o.shape[i] = (int64_t)shape[i];
@@ -422,6 +486,7 @@ struct ProgramBuilder {
     sig.push_back('O');
     put(node);
     put(mode);
+    put(addend);
     put(o.dtype);
     put_shape(shape);
     sig.push_back(((uintptr_t)ptr & 15u) == 0 ? 'a' : 'u');
@@ -478,8 +543,9 @@ struct Request {
   std::vector<size_t> iter;
   int mode;
   ImplPtr expr;                  // expression root (for STORE / ACCUM) or reduce input
-  std::vector<ImplPtr> chain;    // STORE: ADD chain of these terms (if non-empty)
+  std::vector<ImplPtr> chain;    // ADD chain of these terms instead of expr (if non-empty)
   TensorImpl* target;
+  std::vector<ImplPtr> addend;   // REDUCE: elementwise terms added to the sum
 };
 
 // Sum over axes by successive keep-dim lmpb_reduce calls (the fallback of a
@@ -518,23 +584,10 @@ void run_requests(std::vector<Request>& reqs) {
     auto& g = groups[iter];
     ProgramBuilder pb;
     for (Request* r : g) {
-      int node;
-      if (!r->chain.empty()) {
-        node = pb.visit(r->chain[0].get());
-        for (size_t i = 1; i < r->chain.size(); ++i) {
-          lmpb_fnode n{};
-          n.kind = LMPB_FN_BINARY;
-          n.sub = LMPB_ADD;
-          n.dtype = (int)r->target->dtype;
-          n.a = node;
-          n.b = pb.visit(r->chain[i].get());
-          node = pb.add_node(n);
-        }
-      } else {
-        node = pb.visit(r->expr.get());
-      }
+      const int node = r->chain.empty() ? pb.visit(r->expr.get()) : pb.chain(r->chain, r->target->dtype);
+      const int addend = r->addend.empty() ? -1 : pb.chain(r->addend, r->target->dtype);
       const std::vector<size_t>& oshape = (r->mode >= LMPB_OUT_REDUCE_SUM) ? r->target->shape : iter;
-      pb.output(node, r->mode, r->target->dtype, oshape, r->target->storage->ptr);
+      pb.output(node, r->mode, r->target->dtype, oshape, r->target->storage->ptr, addend);
     }
     lmpb_status st = run_program(pb, iter);
     if (st == LMPB_ERR_UNSUPPORTED) {
@@ -558,9 +611,17 @@ void run_requests(std::vector<Request>& reqs) {
           p1.output(node, r->mode, r->target->dtype, iter, r->target->storage->ptr);
           LMPB_OK_OR_THROW(run_program(p1, iter));
         } else {
-          ImplPtr full = new_impl(iter, r->expr->dtype, DeviceType::CUDA, true);
+          if (!r->addend.empty()) {  // the elementwise part first, then accumulate the reduction
+            ProgramBuilder p0;
+            p0.output(p0.chain(r->addend, r->target->dtype), LMPB_OUT_STORE, r->target->dtype, r->target->shape,
+                      r->target->storage->ptr);
+            LMPB_OK_OR_THROW(run_program(p0, r->target->shape));
+            r->mode = LMPB_OUT_REDUCE_SUM_ACCUM;
+          }
+          ImplPtr full = new_impl(iter, r->target->dtype, DeviceType::CUDA, true);
           ProgramBuilder p1;
-          p1.output(p1.visit(r->expr.get()), LMPB_OUT_STORE, full->dtype, iter, full->storage->ptr);
+          const int rn = r->chain.empty() ? p1.visit(r->expr.get()) : p1.chain(r->chain, r->target->dtype);
+          p1.output(rn, LMPB_OUT_STORE, full->dtype, iter, full->storage->ptr);
           LMPB_OK_OR_THROW(run_program(p1, iter));
           ImplPtr red = reduce_to_shape_eager(full, r->target->shape);
           void* dst = r->target->storage->ptr;
@@ -625,6 +686,18 @@ void realize_all(const std::vector<ImplPtr>& ts) {
     }
     std::vector<ImplPtr> elem, red;
     for (auto& x : terms) (is_reduce_term(x) ? red : elem).push_back(x);
+    bool one_space = true;
+    for (auto& x : red) one_space &= x->lazy->inputs[0]->shape == red[0]->lazy->inputs[0]->shape;
+    if (one_space) {
+      // target = (elementwise terms) + sum(reduce inputs): one output of the
+      // kernel that walks the reduce inputs' iteration space
+      std::vector<ImplPtr> ins;
+      for (auto& x : red) ins.push_back(x->lazy->inputs[0]);
+      Request rq{ins[0]->shape, LMPB_OUT_REDUCE_SUM, nullptr, ins, t.get(), elem};
+      reqs.push_back(rq);
+      done.push_back(t);
+      continue;
+    }
     // The elementwise part must not be ordered after the reductions when it
     // overwrites the target: give the target its elementwise value first
     // (zero-filled when there is none), then accumulate every reduction.
