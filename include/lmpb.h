@@ -151,6 +151,21 @@ lmpb_status lmpb_unary(int op, int dtype, const void* in, void* out, int64_t n, 
 lmpb_status lmpb_reduce(int op, int dtype, const void* in, const int64_t* shape, int ndim,
                         int axis, void* out, void* stream);
 
+/* lmpb_reduce for callers that must not allocate device memory during the
+ * call (a framework whose memory planner owns every allocation, a runtime
+ * with a fixed device budget, a loop that cannot risk a pool miss turning
+ * into cudaMalloc).  Same arguments and results as lmpb_reduce, but the
+ * split-row workspace is a fixed 4 MiB scratch array inside the library,
+ * held on every GPU that loads it until the process exits; nothing is
+ * allocated or freed.  A reduction needing more than 4 MiB of scratch
+ * (outer x inner x chunks x element size) returns LMPB_ERR_INVALID.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls share the one array:
+ * calls whose kernels may overlap on the GPU (other streams, other host
+ * threads) race on it, so serialise them.  No counterpart in the reference. */
+lmpb_status lmpb_reduce_noalloc(int op, int dtype, const void* in, const int64_t* shape, int ndim,
+                                int axis, void* out, void* stream);
+
 /* ----------------------------------------------------------- matmul */
 
 /* C[m,n] = A[m,k] · B[k,n], row-major, converted to out_dtype

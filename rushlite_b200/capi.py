@@ -41,7 +41,7 @@ EXPORTS = [
     "lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_broadcast_shape", "lmpb_binary", "lmpb_unary",
     "lmpb_reduce", "lmpb_matmul", "lmpb_gemm_f32", "lmpb_transpose", "lmpb_malloc", "lmpb_free",
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
-    "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error",
+    "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error", "lmpb_reduce_noalloc",
 ]
 
 
@@ -82,6 +82,7 @@ def lib() -> C.CDLL:
         L.lmpb_binary.argtypes = [i32, i32, vp, i32, P64, i32, vp, i32, P64, i32, vp, d, d, vp]
         L.lmpb_unary.argtypes = [i32, i32, vp, vp, i64, d, d, vp]
         L.lmpb_reduce.argtypes = [i32, i32, vp, P64, i32, i32, vp, vp]
+        L.lmpb_reduce_noalloc.argtypes = [i32, i32, vp, P64, i32, i32, vp, vp]
         L.lmpb_matmul.argtypes = [i32, vp, i32, vp, i32, vp, i64, i64, i64, vp]
         L.lmpb_gemm_f32.argtypes = [i32, i32, vp, vp, vp, i64, i64, i64, C.c_float, vp]
         L.lmpb_transpose.argtypes = [i32, vp, vp, i64, i64, vp]

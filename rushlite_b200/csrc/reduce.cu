@@ -302,6 +302,16 @@ lmpb_status reduce_geometry(const int64_t* shape, int ndim, int axis, int64_t& o
   return LMPB_OK;
 }
 
+// Workspace bytes lmpb_reduce would need for this call (0 when none).
+size_t reduce_workspace_bytes(int dtype, const void* in, const void* out, const int64_t* shape, int ndim,
+                              int axis) {
+  int64_t outer, R, inner;
+  if (!valid_dtype(dtype) || reduce_geometry(shape, ndim, axis, outer, R, inner) != LMPB_OK) return 0;
+  if (outer * inner == 0 || R == 0) return 0;
+  LMPB_DISPATCH_DTYPE(dtype, T, return plan_reduce<T>(in, out, outer, R, inner).ws_bytes);
+  return 0;
+}
+
 // Runs a planned reduction with a caller-provided workspace of at least
 // plan.ws_bytes (may be null when ws_bytes == 0).
 lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64_t* shape,

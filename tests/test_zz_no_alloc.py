@@ -1,0 +1,51 @@
+"""lmpb_reduce_noalloc: the reduction entry point for callers that may not
+allocate device memory while it runs (their own memory planner owns all
+allocations, or a pool miss must never turn into a cudaMalloc).  It must give
+the same results as lmpb_reduce, call after call, while keeping its split
+workspace in the library's fixed scratch array.
+
+This file is named so that pytest collects it last."""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from rushlite_b200 import capi
+from tests.util import assert_bitexact, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(op, dt, in_ptr, shape, axis, out_ptr):
+    capi.check(capi.lib().lmpb_reduce_noalloc(op, dt, in_ptr, capi.shape_arr(shape), len(shape), axis,
+                                              out_ptr, None))
+
+
+# [16384, 4096] axis 0 uses the split-row workspace (the C3 column case)
+CASES = [((16384, 4096), 0, np.float32), ((16384, 4096), 0, np.int32), ((4096, 3000), 0, np.float32),
+         ((2048, 1024), 1, np.float32)]
+
+
+@pytest.mark.parametrize("shape,axis,dt", CASES)
+def test_noalloc_matches_lmpb_reduce_twice(cuda, shape, axis, dt):
+    torch = cuda
+    rng = np.random.default_rng(17)
+    dtc = {np.float32: capi.FLOAT32, np.int32: capi.INT32}[dt]
+    for call in range(2):  # two calls in a row: the shared scratch keeps the last call's contents
+        x = (rng.standard_normal(shape) if dt == np.float32 else rng.integers(-1000, 1001, shape)).astype(dt)
+        dx = torch.from_numpy(x).cuda()
+        oshape = list(shape)
+        oshape[axis] = 1
+        for op in (capi.SUM, capi.MAX, capi.MIN):
+            ref_out = torch.zeros(oshape, dtype=dx.dtype, device="cuda")
+            got_out = torch.full(oshape, 7, dtype=dx.dtype, device="cuda")
+            capi.reduce(op, dtc, dx.data_ptr(), shape, axis, ref_out.data_ptr())
+            _noalloc(op, dtc, dx.data_ptr(), shape, axis, got_out.data_ptr())
+            torch.cuda.synchronize()
+            want, got = ref_out.cpu().numpy(), got_out.cpu().numpy()
+            # same plan and summation order as lmpb_reduce: identical results
+            assert_bitexact(got, want, f"call {call} op {op} {shape} ax{axis}")
+            assert rel_err(got, want) <= 1e-5
+
