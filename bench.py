@@ -35,6 +35,16 @@ ROWS, COLS = 8192, 8192
 FWD_BYTES = ROWS * COLS * 4 * 2 + ROWS * 4            # read a, write d, read b
 BWD_BYTES = ROWS * COLS * 4 * 3 + ROWS * 4 * 3        # read a, RMW grad_a, read b, RMW grad_b
 STEP_BYTES = FWD_BYTES + BWD_BYTES
+
+
+def set_rows(rows: int) -> None:
+    """Row count of a (default 8192, the C2 config); smaller values are for
+    profiling captures that must stay small."""
+    global ROWS, FWD_BYTES, BWD_BYTES, STEP_BYTES
+    ROWS = rows
+    FWD_BYTES = ROWS * COLS * 4 * 2 + ROWS * 4
+    BWD_BYTES = ROWS * COLS * 4 * 3 + ROWS * 4 * 3
+    STEP_BYTES = FWD_BYTES + BWD_BYTES
 METRIC = "fused elementwise/reduction HBM GB/s (C2 broadcast chain fwd+bwd)"
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 
@@ -212,7 +222,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--rows", type=int, default=8192, help="rows of a (8192 = the C2 config; smaller for profiling)")
     args = ap.parse_args()
+    set_rows(args.rows)
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
 
