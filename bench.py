@@ -214,6 +214,190 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# Secondary workloads (C3, C4, C5).  The default run is
+# C2 above; these print one JSON line each with their own metric.
+
+def _events(torch):
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _time(torch, fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = _events(torch)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def workload_c3(rsl, torch, args):
+    """Dim-wise reductions of fp32 N(0,1) and int32 U{-1000..1000} [16384, 4096], plus the
+    backward of sum (grad_a += broadcast of g).  GB/s = algorithmic bytes / event time."""
+    R, C = 16384, 4096
+    rng = np.random.default_rng(3)
+    xf = rsl.Variable(rng.standard_normal((R, C), dtype=np.float32), requires_grad=True)
+    xi = rsl.Variable(rng.integers(-1000, 1001, (R, C)).astype(np.int32), dtype=rsl.dtype.int32)
+    nbytes = R * C * 4
+    res, tot_b, tot_ms = {}, 0, 0.0
+    for name, x, fn in [("sum", xf, rsl.sum), ("max", xf, rsl.max), ("min", xf, rsl.min), ("int32_sum", xi, rsl.sum)]:
+        for axis in (0, 1):
+            out_b = (C if axis == 0 else R) * 4
+            ms = _time(torch, lambda: fn(x, axis).realize(), args.steps)
+            res[f"{name}_dim{axis}"] = {"ms": ms, "GB/s": (nbytes + out_b) / ms / 1e6}
+            tot_b += nbytes + out_b
+            tot_ms += ms
+    for axis in (0, 1):  # sum backward: RMW of grad_a (+ read of g)
+        def bw():
+            s = rsl.sum(xf, axis)
+            e0, e1 = _events(torch)
+            e0.record()
+            s.backward()
+            e1.record()
+            return e0, e1
+        for _ in range(3):
+            bw()
+        evs = [bw() for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+        res[f"sum_backward_dim{axis}"] = {"ms": ms, "GB/s": 2 * nbytes / ms / 1e6}
+        tot_b += 2 * nbytes
+        tot_ms += ms
+    peak, src = peak_hbm()
+    value = tot_b / tot_ms / 1e6
+    return {"metric": "dim-wise reduction HBM GB/s (C3, all ops)", "value": value, "unit": "GB/s",
+            "higher_is_better": True, "dtype": "f32/i32", "config": {"workload": "C3 reductions", "shape": [R, C]},
+            "ops": res, "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s",
+                                     "frac": value / peak, "peak_source": src}}
+
+
+def workload_c4(rsl, torch, args):
+    """fp32 matmul sweep through the public API, forward and dA/dB (3 GEMMs, 6MNK flops)."""
+    out, tot_f, tot_ms = {}, 0.0, 0.0
+    for (m, k, n) in [(1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (32768, 4096, 4096)]:
+        rng = np.random.default_rng(m + k + n)
+        A = rsl.Variable((rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32), requires_grad=True)
+        B = rsl.Variable((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32), requires_grad=True)
+        it = max(2, min(args.steps, int(2e13 / (m * n * k))))
+        fwd = _time(torch, lambda: rsl.matmul(A, B).realize(), it)
+        step = _time(torch, lambda: rsl.matmul(A, B).backward(), it)
+        out[f"{m}x{k}x{n}"] = {"fwd_ms": fwd, "fwd_TFLOPs": 2 * m * n * k / fwd / 1e9,
+                               "fwd_bwd_ms": step, "fwd_bwd_TFLOPs": 6 * m * n * k / step / 1e9}
+        tot_f += 6 * m * n * k
+        tot_ms += step
+    try:
+        bf16 = float(json.load(open(PEAKS))["bf16_tflops"])
+    except Exception:
+        bf16 = 1590.0
+    tf32 = bf16 / 2  # dense TF32 issues at half the bf16 rate
+    value = tot_f / tot_ms / 1e9
+    return {"metric": "fp32 (3xTF32) matmul TFLOP/s, fwd + dA + dB (C4 sweep)", "value": value, "unit": "TFLOP/s",
+            "higher_is_better": True, "dtype": "f32 (3xTF32 on tcgen05)", "config": {"workload": "C4 matmul sweep"},
+            "shapes": out,
+            "roofline": {"bound": "tensor", "achieved": value, "peak": tf32 / 3, "unit": "TFLOP/s",
+                         "frac": value / (tf32 / 3),
+                         "peak_source": "measured bf16 GEMM / 2 (dense TF32) / 3 (three MMAs per product)"}}
+
+
+def _mlp_params(rsl, dims, seed=5):
+    rng = np.random.default_rng(seed)
+    ps = []
+    for i in range(len(dims) - 1):
+        w = (rng.standard_normal((dims[i], dims[i + 1])) / np.sqrt(dims[i])).astype(np.float32)
+        b = (rng.standard_normal((dims[i + 1],)) / np.sqrt(dims[i])).astype(np.float32)
+        ps += [rsl.Variable(w, requires_grad=True), rsl.Variable(b, requires_grad=True)]
+    return ps
+
+
+def _mlp_step(rsl, ps, x, y, lr, allreduce=None):
+    import sys as _s
+
+    with rsl.capture_on():
+        h = x
+        n = len(ps) // 2
+        for i in range(n):
+            h = rsl.matmul(h, ps[2 * i]) + ps[2 * i + 1]
+            if i < n - 1:
+                h = rsl.clamp(h, 0, _s.float_info.max)
+        m = rsl.max(h, 1)
+        e = rsl.exp(h - m)
+        p = e / rsl.sum(e, 1)
+    loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
+    loss.backward()
+    if allreduce is not None:
+        allreduce([q.grad for q in ps])
+    with rsl.no_grad():
+        return [rsl.Variable(q.data - lr * q.grad, True) for q in ps], loss
+
+
+def workload_c5(rsl, torch, args, rank, world, pg):
+    """Data-parallel MLP: Linear(4096,4096)+ReLU x4, Linear(4096,1000)+Softmax, fp32, global
+    batch 8192 split over the ranks; gradients summed with NCCL all-reduce (the loss is a sum)."""
+    dims = [4096] * 5 + [1000]
+    gb = 8192
+    bl = gb // world
+    rng = np.random.default_rng(100 + rank)
+    x = rsl.Variable(rng.standard_normal((bl, 4096), dtype=np.float32))
+    lab = rng.integers(0, 1000, bl)
+    yn = np.zeros((bl, 1000), np.float32)
+    yn[np.arange(bl), lab] = 1
+    y = rsl.Variable(yn)
+    ps = _mlp_params(rsl, dims)
+
+    def allreduce(grads):
+        for g in grads:
+            pg.all_reduce(torch.as_tensor(g, device="cuda"))
+
+    ar = allreduce if world > 1 else None
+    for _ in range(args.warmup):
+        ps, _l = _mlp_step(rsl, ps, x, y, 1e-4, ar)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    e0, e1 = _events(torch)
+    e0.record()
+    steps = min(args.steps, 50)
+    for _ in range(steps):
+        ps, loss = _mlp_step(rsl, ps, x, y, 1e-4, ar)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if pg:
+        t = torch.tensor([ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 3.225e12  # GEMM flops per global step
+    return {"metric": "DP MLP train steps/s (C5)", "value": 1e3 / ms, "unit": "steps/s", "n_gpus": world,
+            "steps": steps, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "dtype": "f32",
+            "config": {"workload": "C5 DP MLP 4x(4096x4096)+4096x1000", "global_batch": gb,
+                       "parallelism": f"dp{world}", "allreduce": "NCCL sum per parameter after backward"},
+            "loss": float(loss.numpy().ravel()[0]), "tflops_total": flops / (ms / 1e3) / 1e12}
+
+
+def workload_c1(rsl, torch, args):
+    """README MLP 256-64-10 ReLU Softmax, batch 32, capture forward, SGD 1e-3."""
+    rng = np.random.default_rng(0)
+    x = rsl.Variable(rng.random((32, 256), dtype=np.float32))
+    y = rsl.Variable(rng.random((32, 10), dtype=np.float32))
+    ps = _mlp_params(rsl, [256, 64, 10])
+    for _ in range(10):
+        ps, _l = _mlp_step(rsl, ps, x, y, 1e-3)
+    torch.cuda.synchronize()
+    steps = 1000
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ps, loss = _mlp_step(rsl, ps, x, y, 1e-3)
+    lv = float(loss.numpy().ravel()[0])
+    dt = time.perf_counter() - t0
+    return {"metric": "README MLP train steps/s (C1)", "value": steps / dt, "unit": "steps/s",
+            "higher_is_better": True, "dtype": "f32", "config": {"workload": "C1 README MLP, batch 32, 1000 steps"},
+            "launches_per_step": None, "final_loss": lv}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -223,6 +407,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--rows", type=int, default=8192, help="rows of a (8192 = the C2 config; smaller for profiling)")
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="c2 (default) is the headline; the others are the secondary BASELINE configs")
     args = ap.parse_args()
     set_rows(args.rows)
     args.warmup = max(args.warmup, 3)
@@ -244,6 +430,20 @@ def main():
     import rushlite_b200 as rsl
 
     rsl.cuda.set_device(local)
+    if args.workload != "c2":
+        if args.workload == "c5":
+            line = workload_c5(rsl, torch, args, rank, world, pg)
+        elif rank == 0:
+            l0 = rsl.cuda.kernel_launches()
+            line = {"c1": workload_c1, "c3": workload_c3, "c4": workload_c4}[args.workload](rsl, torch, args)
+            line["gpu_launches_total"] = int(rsl.cuda.kernel_launches() - l0)
+        if rank == 0:
+            line.setdefault("n_gpus", world)
+            line["data"] = "synthetic (seeded)"
+            print(json.dumps(line), flush=True)
+        if pg:
+            pg.destroy_process_group()
+        return
     a_np, b_np = inputs(rank)
     a = rsl.Variable(a_np, requires_grad=True, device=rsl.device.cuda)
     b = rsl.Variable(b_np, requires_grad=True, device=rsl.device.cuda)

@@ -190,6 +190,23 @@ PYBIND11_MODULE(_C, m) {
       .def("tolist", [](const Tensor& t) { return t.to_vector(); })
       .def("numpy", [](const Tensor& t, py::object out) { return to_numpy(t, out); }, py::arg("out") = py::none())
       .def("data_ptr", [](Tensor& t) { return reinterpret_cast<uintptr_t>(t.data()); })
+      // zero-copy view for other CUDA libraries (torch.as_tensor, NCCL through torch.distributed);
+      // realizes the tensor; work on it is ordered on the backend's stream
+      .def_property_readonly("__cuda_array_interface__", [](Tensor& t) {
+        if (t.device() != DeviceType::CUDA) throw py::attribute_error("not a CUDA tensor");
+        static const char* ts[] = {"|b1", "<i2", "<i4", "<i8", "<f4", "<f8"};
+        py::tuple shape(t.shape().size());
+        for (size_t i = 0; i < t.shape().size(); ++i) shape[i] = t.shape()[i];
+        py::dict d;
+        d["shape"] = shape;
+        d["typestr"] = ts[static_cast<int>(t.type())];
+        d["data"] = py::make_tuple(reinterpret_cast<uintptr_t>(t.data()), false);
+        d["version"] = 3;
+        d["strides"] = py::none();
+        uintptr_t s = reinterpret_cast<uintptr_t>(lmp::tensor::current_stream());
+        d["stream"] = s == 0 ? py::object(py::int_(1)) : py::object(py::int_(s));  // 1 = legacy default stream
+        return d;
+      })
       .def("__repr__", [](const Tensor& t) {
         std::ostringstream os;
         os << t;
