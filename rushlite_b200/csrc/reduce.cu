@@ -164,19 +164,15 @@ __global__ void __launch_bounds__(kThreads)
   for (int j = 0; j < VW; ++j) acc[j] = Rd::identity();
   if constexpr (VW > 1) {
     int64_t r = r0;
-    for (; r + 3 < r1; r += 4) {
-      V16<T> x0, x1, x2, x3;
-      x0.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 0) * inner));
-      x1.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 1) * inner));
-      x2.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 2) * inner));
-      x3.raw = __ldg(reinterpret_cast<const uint4*>(base + (r + 3) * inner));
+    // 8 rows of loads in flight per thread before the (in-order) accumulation
+    for (; r + 7 < r1; r += 8) {
+      V16<T> x[8];
 #pragma unroll
-      for (int j = 0; j < VW; ++j) {
-        acc[j] = Rd::apply(acc[j], x0.v[j]);
-        acc[j] = Rd::apply(acc[j], x1.v[j]);
-        acc[j] = Rd::apply(acc[j], x2.v[j]);
-        acc[j] = Rd::apply(acc[j], x3.v[j]);
-      }
+      for (int u = 0; u < 8; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u) * inner));
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
     }
     for (; r < r1; ++r) {
       V16<T> x;
@@ -220,7 +216,7 @@ template <typename T>
 int64_t pick_chunks(int64_t outer, int64_t R, int64_t inner, int vw) {
   const int64_t colblocks = (inner / vw + kThreads - 1) / kThreads;
   const int64_t ctas = colblocks * outer;
-  const int64_t target = (int64_t)sm_count() * 4;
+  const int64_t target = (int64_t)sm_count() * 8;
   if (ctas >= target || R < 64) return 1;
   int64_t S = (target + ctas - 1) / ctas;
   if (S > R / 16) S = R / 16;  // keep >= 16 rows per chunk

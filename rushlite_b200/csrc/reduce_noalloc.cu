@@ -8,7 +8,7 @@
 // device budget, or a real-time loop that must not hit a pool miss that ends
 // in cudaMalloc).  This variant uses instead one fixed scratch array that
 // lives in the library's device data for as long as the library is loaded,
-// on every GPU that loads it (4 MiB each).
+// on every GPU that loads it (8 MiB each).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -26,10 +26,10 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
 
 namespace {
 
-// The split plan targets 4 CTAs per SM with 16-byte column vectors, so its
-// workspace is at most about 4 x SMs x 256 threads x 16 B (2.4 MB on a
-// 148-SM B200); 4 MiB covers it with margin.
-constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB per device
+// The split plan targets 8 CTAs per SM with 16-byte column vectors, so its
+// workspace is at most about 8 x SMs x 256 threads x 16 B (4.9 MB on a
+// 148-SM B200); 8 MiB covers it with margin.
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
 
 // The scratch itself.  Host code must not pass `g_noalloc_scratch` to a
 // kernel: on the host the name is only a stand-in for the symbol, not a
