@@ -425,6 +425,9 @@ def main():
     if world > 1:
         import torch.distributed as dist
 
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
+
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
         pg = dist
     import rushlite_b200 as rsl

@@ -228,7 +228,11 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
     }
   }
   const int64_t inner = p.size[p.G - 1];
-  int want = p.pattern == kElementwise ? 8 : 4;
+  int want = p.pattern == kElementwise ? 4 : 8;  // measured best on B200 (C2 sweep)
+  if (const char* e = getenv(p.pattern == kElementwise ? "LMPB_FUSED_VEC_EW" : "LMPB_FUSED_VEC_RED")) {
+    const int v = atoi(e);  // tuning override: 1, 2, 4, 8 or 16
+    if (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) want = v;
+  }
   p.vec = 1;
   for (int v = want; v > 1; v >>= 1)
     if (inner % v == 0) { p.vec = v; break; }
