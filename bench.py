@@ -222,11 +222,18 @@ def _events(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
+def _backlog(torch, ms=20.0):
+    """Queues a sleep kernel so the launches that follow pile up behind it:
+    the events after it then time device work only, not host launch gaps."""
+    torch.cuda._sleep(int(ms * 1e-3 * 1.9e9))
+
+
 def _time(torch, fn, iters, warmup=3):
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     e0, e1 = _events(torch)
+    _backlog(torch)
     e0.record()
     for _ in range(iters):
         fn()
@@ -261,6 +268,8 @@ def workload_c3(rsl, torch, args):
             return e0, e1
         for _ in range(3):
             bw()
+        torch.cuda.synchronize()
+        _backlog(torch)
         evs = [bw() for _ in range(args.steps)]
         torch.cuda.synchronize()
         ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))

@@ -525,23 +525,39 @@ struct Gen {
     os << "}\n";
   }
 
+  // Split-row partials -> outputs.  A CTA owns 32 adjacent columns; its 8 warps
+  // each sum a contiguous run of chunks (8 loads in flight), and warp 0 folds
+  // the 8 runs in order: deterministic, and not latency-bound on long S.
   void gen_combine(const std::string& name) {
     const int64_t Q = p.size[1];
+    const int64_t per = (p.S + 7) / 8;
     os << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ") " << name << "(const Params prm) {\n";
-    os << "  for (unsigned long long q = blockIdx.x * " << kThreads << "ull + threadIdx.x; q < " << Q
-       << "ull; q += gridDim.x * " << kThreads << "ull) {\n";
+    os << "  const unsigned lane = threadIdx.x & 31u, w = threadIdx.x >> 5;\n";
+    os << "  const unsigned long long q = blockIdx.x * 32ull + lane;\n";
+    os << "  const int s0 = (int)w * " << per << ", s1 = s0 + " << per << " < " << p.S << " ? s0 + " << per << " : " << p.S << ";\n";
     for (size_t j = 0; j < h.outs.size(); ++j) {
       if (p.out_mode[j] < LMPB_OUT_REDUCE_SUM) continue;
       const std::string OT = tname(h.outs[j].dtype);
-      os << "    { const " << OT << "* W = reinterpret_cast<const " << OT << "*>(static_cast<const char*>(prm.ws) + " << h.ws_offset[j] << "ull);\n";
-      os << "      " << OT << "* O = static_cast<" << OT << "*>(prm.out[" << j << "]);\n";
-      os << "      " << OT << " a = W[q];\n      for (int s = 1; s < " << p.S << "; ++s) a = lmpb_dev::r_add<" << OT << ">(a, W[s * " << Q << "ull + q]);\n";
+      const std::string J = std::to_string(j);
+      os << "  { __shared__ " << OT << " run" << J << "[8][32];\n";
+      os << "    const " << OT << "* W = reinterpret_cast<const " << OT << "*>(static_cast<const char*>(prm.ws) + " << h.ws_offset[j] << "ull);\n";
+      os << "    " << OT << " a = 0;\n";
+      os << "    if (q < " << Q << "ull) {\n      int s = s0;\n";
+      os << "      for (; s + 7 < s1; s += 8) { " << OT << " v[8];\n";
+      os << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) v[u] = W[(unsigned long long)(s + u) * " << Q << "ull + q];\n";
+      os << "        #pragma unroll\n        for (int u = 0; u < 8; ++u) a = lmpb_dev::r_add<" << OT << ">(a, v[u]); }\n";
+      os << "      for (; s < s1; ++s) a = lmpb_dev::r_add<" << OT << ">(a, W[(unsigned long long)s * " << Q << "ull + q]);\n    }\n";
+      os << "    run" << J << "[w][lane] = a;\n    __syncthreads();\n";
+      os << "    if (w == 0 && q < " << Q << "ull) { " << OT << " r = run" << J << "[0][lane];\n";
+      os << "      #pragma unroll\n      for (int k = 1; k < 8; ++k) r = lmpb_dev::r_add<" << OT << ">(r, run" << J << "[k][lane]);\n";
+      os << "      " << OT << "* O = static_cast<" << OT << "*>(prm.out[" << J << "]);\n";
       if (p.out_mode[j] == LMPB_OUT_REDUCE_SUM_ACCUM)
-        os << "      O[q] = lmpb_dev::r_add<" << OT << ">(O[q], a); }\n";
+        os << "      O[q] = lmpb_dev::r_add<" << OT << ">(O[q], r);\n";
       else
-        os << "      O[q] = a; }\n";
+        os << "      O[q] = r;\n";
+      os << "    }\n    __syncthreads();\n  }\n";
     }
-    os << "  }\n}\n";
+    os << "}\n";
   }
 };
 
@@ -892,8 +908,7 @@ extern "C" lmpb_status lmpb_fused_launch(lmpb_fused h, const void* const* leaf_p
     return cu_err(r, "cuLaunchKernel(fused)");
   }
   if (p.pattern == kColReduce && p.S > 1) {
-    int64_t b = (p.size[1] + kThreads - 1) / kThreads;
-    unsigned g2 = (unsigned)std::max<int64_t>(1, std::min(b, cap));
+    const unsigned g2 = (unsigned)((p.size[1] + 31) / 32);
     r = drv().launchKernel(fns[2], g2, 1, 1, kThreads, 1, 1, 0, reinterpret_cast<CUstream>(stream), nullptr, config);
     lmpb::count_launch();
     if (r != CUDA_SUCCESS) {

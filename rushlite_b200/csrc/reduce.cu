@@ -190,16 +190,38 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Combines S chunk partials in chunk order: out[i] = op over s of part[s][i].
+// Combines S chunk partials: out[i] = op over s of part[s][i], in chunk order.
+// A CTA owns 32 adjacent columns (lane = column, coalesced); its 8 warps take
+// 8 contiguous runs of chunks, each with 8 independent loads in flight, and
+// warp 0 folds the 8 run results in run order through shared memory.
 template <int OP, typename T>
 __global__ void __launch_bounds__(kThreads)
     reduce_combine_kernel(const T* __restrict__ part, T* __restrict__ out, int64_t n, int S) {
   using Rd = RedOp<OP, T>;
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * kThreads) {
-    T acc = part[i];
-    for (int s = 1; s < S; ++s) acc = Rd::apply(acc, part[(int64_t)s * n + i]);
-    out[i] = acc;
+  __shared__ T run[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t i = (int64_t)blockIdx.x * 32 + lane;
+  const int per = (S + 7) / 8;
+  const int s0 = w * per, s1 = min(S, s0 + per);
+  T acc = Rd::identity();
+  if (i < n) {
+    int s = s0;
+    for (; s + 7 < s1; s += 8) {
+      T v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[(int64_t)(s + u) * n + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = Rd::apply(acc, v[u]);
+    }
+    for (; s < s1; ++s) acc = Rd::apply(acc, part[(int64_t)s * n + i]);
+  }
+  run[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && i < n) {
+    T r = run[0][lane];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) r = Rd::apply(r, run[k][lane]);
+    out[i] = r;
   }
 }
 
@@ -281,8 +303,9 @@ static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, c
     reduce_cols_kernel<OP, T, 1><<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
   lmpb_status s = launch_status("reduce_cols_kernel");
   if (s != LMPB_OK || p.S == 1) return s;
-  int g2 = (int)std::min<int64_t>((nout + kThreads - 1) / kThreads, (int64_t)sm_count() * 8);
-  reduce_combine_kernel<OP, T><<<g2, kThreads, 0, st>>>(ws, out, nout, (int)p.S);
+  const int64_t g2 = (nout + 31) / 32;
+  if (g2 > 0x7FFFFFFFll) return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce: output too large to combine");
+  reduce_combine_kernel<OP, T><<<(unsigned)g2, kThreads, 0, st>>>(ws, out, nout, (int)p.S);
   return launch_status("reduce_combine_kernel");
 }
 
