@@ -11,11 +11,14 @@
 //    K contiguous fp32, K padded to the k-block), transposing op(A) / op(B)
 //    on the way when the caller's layout is not K-major.  It reads each input
 //    element once and writes 8 bytes; for 4096^3 that is ~1.5% of the GEMM.
-// 2. The GEMM kernel: one CTA per 128 x BN output tile, 6 warps:
+// 2. The GEMM kernel: persistent, one CTA per SM walking 128 x BN output
+//    tiles in grouped order, 6 warps:
 //      warp 0     TMA producer (one elected thread): 4 tiles per k-block
 //                 (A hi/lo, B hi/lo) into a STAGES-deep shared-memory ring,
-//                 128-byte swizzled, completion on an mbarrier;
-//      warp 1     owns the TMEM accumulator (128 lanes x BN fp32 columns) and
+//                 64-byte swizzled, completion on an mbarrier;
+//      warp 1     owns two TMEM accumulators (128 lanes x BN fp32 columns
+//                 each; the epilogue drains one while the MMAs fill the
+//                 other) and
 //                 issues the tcgen05.mma.kind::tf32 instructions (one thread),
 //                 3 products x BK/8 MMAs per k-block, then tcgen05.commit
 //                 frees the stage;
@@ -45,12 +48,13 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int BK = 32;      // 32 fp32 = 128 bytes per row = one 128B swizzle atom
-constexpr int STAGES = 2;
+constexpr int BK = 16;      // 16 fp32 = 64 bytes per row = one 64B swizzle atom
+constexpr int STAGES = 4;
 constexpr int kThreads = 192;
-constexpr int A_TILE = BM * BK * 4;  // 16 KB
-constexpr int B_TILE = BN * BK * 4;  // 32 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+constexpr int A_TILE = BM * BK * 4;  // 8 KB
+constexpr int B_TILE = BN * BK * 4;  // 16 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
+constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i overlaps MMAs of tile i+1
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
 
@@ -69,6 +73,10 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
@@ -101,14 +109,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// K-major, 128B-swizzled tile: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+// K-major, 64B-swizzled tile: rows of 64 bytes, 8-row atoms 512 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   uint64_t d = 0;
   d |= (uint64_t)((addr & 0x3FFFF) >> 4);  // start address
   d |= (uint64_t)1 << 16;                  // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;        // stride byte offset: next 8-row group
+  d |= (uint64_t)(512 >> 4) << 32;         // stride byte offset: next 8-row group
   d |= (uint64_t)1 << 46;                  // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                  // SWIZZLE_128B
+  d |= (uint64_t)4 << 61;                  // SWIZZLE_64B
   return d;
 }
 
@@ -196,40 +204,48 @@ __global__ void __launch_bounds__(256)
 
 // ------------------------------------------------------------ GEMM kernel
 
+// Tile t of a tiles_m x tiles_n grid in grouped order: 8 row-tiles at a time
+// walk the column tiles, so concurrently running CTAs share B panels in L2.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m0, int& n0) {
+  const int group = 8;
+  const int g = t / (group * tiles_n);
+  const int first_m = g * group;
+  const int gsize = min(tiles_m - first_m, group);
+  const int local = t % (group * tiles_n);
+  m0 = (first_m + local % gsize) * BM;
+  n0 = (local / gsize) * BN;
+}
+
+// Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                        const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                       float* __restrict__ C, int M, int N, int num_kb, int beta) {
+                       float* __restrict__ C, int M, int N, int num_kb, int beta, int tiles_m, int tiles_n) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* accum = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + STAGES;  // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // tile rasterisation: groups of 8 row-tiles share B panels in L2
-  const int tiles_n = gridDim.x, tiles_m = gridDim.y;
-  const int tid = blockIdx.y * tiles_n + blockIdx.x;
-  const int group = 8;
-  const int g = tid / (group * tiles_n);
-  const int first_m = g * group;
-  const int gsize = min(tiles_m - first_m, group);
-  const int tm = first_m + (tid % (group * tiles_n)) % gsize;
-  const int tn = (tid % (group * tiles_n)) / gsize;
-  const int m0 = tm * BM, n0 = tn * BN;
+  const int num_tiles = tiles_m * tiles_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    mbar_init(smem_u32(accum), 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 128);  // every epilogue thread arrives
+    }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(BN)
+                 "r"(TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -239,93 +255,121 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer
+    // ---- TMA producer: one ring position per k-block, continuing across tiles
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAh)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAl)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBh)) : "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBl)) : "memory");
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t phase = (kb / STAGES) & 1;
-      if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, 1)) break;
-      uint8_t* st = smem + s * STAGE_BYTES;
-      const uint32_t bar = smem_u32(&full[s]);
-      mbar_expect_tx(bar, STAGE_BYTES);
-      tma_load_2d(smem_u32(st), &tAh, kb * BK, m0, bar);
-      tma_load_2d(smem_u32(st + A_TILE), &tAl, kb * BK, m0, bar);
-      tma_load_2d(smem_u32(st + 2 * A_TILE), &tBh, kb * BK, n0, bar);
-      tma_load_2d(smem_u32(st + 2 * A_TILE + B_TILE), &tBl, kb * BK, n0, bar);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int m0, n0;
+      tile_coords(t, tiles_m, tiles_n, m0, n0);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t phase = (it / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE_BYTES;
+        const uint32_t bar = smem_u32(&full[s]);
+        mbar_expect_tx(bar, STAGE_BYTES);
+        tma_load_2d(smem_u32(st), &tAh, kb * BK, m0, bar);
+        tma_load_2d(smem_u32(st + A_TILE), &tAl, kb * BK, m0, bar);
+        tma_load_2d(smem_u32(st + 2 * A_TILE), &tBh, kb * BK, n0, bar);
+        tma_load_2d(smem_u32(st + 2 * A_TILE + B_TILE), &tBl, kb * BK, n0, bar);
+      }
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer
     constexpr uint32_t idesc = instr_desc();
+    uint32_t it = 0;
     bool ok = true;
-    for (int kb = 0; kb < num_kb && ok; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t phase = (kb / STAGES) & 1;
-      if (!mbar_wait(smem_u32(&full[s]), phase, 2)) {
-        ok = false;
-        break;
-      }
+    int lt = 0;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const uint32_t aphase = (lt >> 1) & 1;
+      if (!mbar_wait(smem_u32(&tempty[acc]), aphase ^ 1, 4)) break;  // epilogue drained this accumulator
       tc_fence_after();
-      const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-      const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_TILE);
-      const uint64_t dBh = smem_desc(base + 2 * A_TILE), dBl = smem_desc(base + 2 * A_TILE + B_TILE);
+      const uint32_t dtm = tmem + (uint32_t)(acc * BN);
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t phase = (it / STAGES) & 1;
+        if (!mbar_wait(smem_u32(&full[s]), phase, 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+        const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_TILE);
+        const uint64_t dBh = smem_desc(base + 2 * A_TILE), dBl = smem_desc(base + 2 * A_TILE + B_TILE);
 #pragma unroll
-      for (int kk = 0; kk < BK / 8; ++kk) {
-        const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
-        const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-        mma_tf32(tmem, dAl + off, dBh + off, idesc, first);  // small terms first
-        mma_tf32(tmem, dAh + off, dBl + off, idesc, 1u);
-        mma_tf32(tmem, dAh + off, dBh + off, idesc, 1u);
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
+          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+          mma_tf32(dtm, dAl + off, dBh + off, idesc, first);  // small terms first
+          mma_tf32(dtm, dAh + off, dBl + off, idesc, 1u);
+          mma_tf32(dtm, dAh + off, dBh + off, idesc, 1u);
+        }
+        mma_commit(smem_u32(&empty[s]));
       }
-      mma_commit(smem_u32(&empty[s]));
+      mma_commit(smem_u32(&tfull[acc]));
     }
-    mma_commit(smem_u32(accum));
   } else if (warp >= 2) {
-    // ---- epilogue: TMEM -> registers -> global
-    const bool ok = mbar_wait(smem_u32(accum), 0, 3);
-    tc_fence_after();
+    // ---- epilogue: TMEM -> registers -> global, one tile behind the MMAs
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = m0 + q * 32 + lane;
-    const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
     const bool vec = (N & 3) == 0;
+    int lt = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const uint32_t aphase = (lt >> 1) & 1;
+      const bool ok = mbar_wait(smem_u32(&tfull[acc]), aphase, 3);
+      tc_fence_after();
+      int m0, n0;
+      tile_coords(t, tiles_m, tiles_n, m0, n0);
+      const int row = m0 + q * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      tmem_ld16(taddr + c, r);
-      if (!ok || row >= M) continue;
-      float* crow = C + (int64_t)row * N + n0 + c;
-      const int ncols = min(16, N - (n0 + c));
-      if (ncols <= 0) continue;
-      if (vec && ncols == 16) {
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        if (!ok || row >= M) continue;
+        float* crow = C + (int64_t)row * N + n0 + c;
+        const int ncols = min(16, N - (n0 + c));
+        if (ncols <= 0) continue;
+        if (vec && ncols == 16) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                 __uint_as_float(r[j + 3]));
-          if (beta) {
-            const float4 o = *reinterpret_cast<const float4*>(crow + j);
-            v.x = __fadd_rn(o.x, v.x);
-            v.y = __fadd_rn(o.y, v.y);
-            v.z = __fadd_rn(o.z, v.z);
-            v.w = __fadd_rn(o.w, v.w);
+          for (int j = 0; j < 16; j += 4) {
+            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                   __uint_as_float(r[j + 3]));
+            if (beta) {
+              const float4 o = *reinterpret_cast<const float4*>(crow + j);
+              v.x = __fadd_rn(o.x, v.x);
+              v.y = __fadd_rn(o.y, v.y);
+              v.z = __fadd_rn(o.z, v.z);
+              v.w = __fadd_rn(o.w, v.w);
+            }
+            *reinterpret_cast<float4*>(crow + j) = v;
           }
-          *reinterpret_cast<float4*>(crow + j) = v;
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) {
-          float v = __uint_as_float(r[j]);
-          if (beta) v = __fadd_rn(crow[j], v);
-          crow[j] = v;
+        } else {
+          for (int j = 0; j < ncols; ++j) {
+            float v = __uint_as_float(r[j]);
+            if (beta) v = __fadd_rn(crow[j], v);
+            crow[j] = v;
+          }
         }
       }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+      if (!ok) break;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -356,7 +400,7 @@ lmpb_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t 
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(LMPB_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return LMPB_OK;
@@ -409,12 +453,15 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   if (s == LMPB_OK) s = make_map(&mBh, Bh, n, Kp, BN);
   if (s == LMPB_OK) s = make_map(&mBl, Bl, n, Kp, BN);
   if (s == LMPB_OK) {
-    dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
-    if (grid.y > 65535) {
-      s = set_error(LMPB_ERR_UNSUPPORTED, "gemm: m too large");
+    const int64_t tiles_n = (n + BN - 1) / BN, tiles_m = (m + BM - 1) / BM;
+    if (tiles_m * tiles_n > 0x7FFFFFFF) {
+      s = set_error(LMPB_ERR_UNSUPPORTED, "gemm: too many tiles");
     } else {
+      const int64_t ntiles = tiles_m * tiles_n;
+      const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
       gemm_3xtf32_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, C, (int)m, (int)n,
-                                                             (int)(Kp / BK), beta != 0.f ? 1 : 0);
+                                                             (int)(Kp / BK), beta != 0.f ? 1 : 0, (int)tiles_m,
+                                                             (int)tiles_n);
       s = launch_status("gemm_3xtf32_kernel");
     }
   }
