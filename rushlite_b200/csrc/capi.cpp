@@ -38,6 +38,31 @@ size_t dtype_size(int dt) {
   return valid_dtype(dt) ? sz[dt] : 0;
 }
 
+// Stream-ordered allocation from the device's default pool.  The first call on
+// a device raises the pool's release threshold so freed blocks stay in the
+// process for reuse instead of being returned to the driver at every
+// synchronisation (which makes the next large allocation map memory again).
+cudaError_t stream_alloc(void** p, size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static std::vector<char> ready;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)ready.size() <= dev) ready.resize(dev + 1, 0);
+    if (!ready[dev]) {
+      cudaMemPool_t pool;
+      if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t keep = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      }
+      ready[dev] = 1;
+    }
+  }
+  return cudaMallocAsync(p, bytes, st);
+}
+
 int sm_count() {
   static std::mutex mu;
   static std::vector<int> cache;

@@ -41,6 +41,9 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 bool valid_dtype(int dt);
 size_t dtype_size(int dt);
 
+// cudaMallocAsync from the device's default pool, kept warm (capi.cpp).
+cudaError_t stream_alloc(void** p, size_t bytes, cudaStream_t st);
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

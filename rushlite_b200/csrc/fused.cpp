@@ -48,6 +48,7 @@ bool valid_dtype(int dt);
 size_t dtype_size(int dt);
 int sm_count();
 void count_launch();
+cudaError_t stream_alloc(void** p, size_t bytes, cudaStream_t st);
 }  // namespace lmpb
 
 using lmpb::set_error;
@@ -875,7 +876,7 @@ extern "C" lmpb_status lmpb_fused_launch(lmpb_fused h, const void* const* leaf_p
   cudaStream_t cst = reinterpret_cast<cudaStream_t>(stream);
   void* ws = nullptr;
   if (h->ws_bytes) {
-    cudaError_t e = cudaMallocAsync(&ws, h->ws_bytes, cst);
+    cudaError_t e = lmpb::stream_alloc(&ws, h->ws_bytes, cst);
     if (e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("fused workspace: ") + cudaGetErrorString(e));
   }
   prm[ob + std::max(1, NO)] = ws;

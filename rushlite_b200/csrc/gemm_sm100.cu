@@ -438,7 +438,7 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   const int64_t Kp = (k + BK - 1) / BK * BK;
   const size_t plane_a = (size_t)m * Kp * 4, plane_b = (size_t)n * Kp * 4;
   void* ws = nullptr;
-  LMPB_CUDA_TRY(cudaMallocAsync(&ws, 2 * plane_a + 2 * plane_b, st));
+  LMPB_CUDA_TRY(stream_alloc((void**)&ws, 2 * plane_a + 2 * plane_b, st));
   float* Ah = static_cast<float*>(ws);
   float* Al = reinterpret_cast<float*>(static_cast<char*>(ws) + plane_a);
   float* Bh = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * plane_a);

@@ -134,7 +134,7 @@ extern "C" lmpb_status lmpb_malloc(void** ptr, size_t bytes, void* stream) {
   LMPB_CHECK_ARG(ptr != nullptr, "lmpb_malloc: null out pointer");
   *ptr = nullptr;
   if (bytes == 0) return LMPB_OK;
-  LMPB_CUDA_TRY(cudaMallocAsync(ptr, bytes, as_stream(stream)));
+  LMPB_CUDA_TRY(stream_alloc((void**)ptr, bytes, as_stream(stream)));
   return LMPB_OK;
 }
 
@@ -201,7 +201,7 @@ extern "C" lmpb_status lmpb_copy(int kind, const void* src, int src_dtype, void*
       return cast_on_device(src, src_dtype, dst, dst_dtype, n, st);
     case LMPB_H2D: {  // raw bytes up, cast on the device
       void* tmp = nullptr;
-      LMPB_CUDA_TRY(cudaMallocAsync(&tmp, sbytes, st));
+      LMPB_CUDA_TRY(stream_alloc((void**)&tmp, sbytes, st));
       LMPB_CUDA_TRY(cudaMemcpyAsync(tmp, src, sbytes, cudaMemcpyHostToDevice, st));
       lmpb_status s = cast_on_device(tmp, src_dtype, dst, dst_dtype, n, st);
       LMPB_CUDA_TRY(cudaFreeAsync(tmp, st));
@@ -209,7 +209,7 @@ extern "C" lmpb_status lmpb_copy(int kind, const void* src, int src_dtype, void*
     }
     case LMPB_D2H: {  // cast on the device, bytes down
       void* tmp = nullptr;
-      LMPB_CUDA_TRY(cudaMallocAsync(&tmp, dbytes, st));
+      LMPB_CUDA_TRY(stream_alloc((void**)&tmp, dbytes, st));
       lmpb_status s = cast_on_device(src, src_dtype, tmp, dst_dtype, n, st);
       if (s != LMPB_OK) return s;
       LMPB_CUDA_TRY(cudaMemcpyAsync(dst, tmp, dbytes, cudaMemcpyDeviceToHost, st));

@@ -349,7 +349,7 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
     void* w = ws;
     if (p.ws_bytes > 0) {
       if (allocate) {
-        LMPB_CUDA_TRY(cudaMallocAsync(&w, p.ws_bytes, st));
+        LMPB_CUDA_TRY(stream_alloc((void**)&w, p.ws_bytes, st));
       } else {
         LMPB_CHECK_ARG(w != nullptr && ws_bytes >= p.ws_bytes, "lmpb_reduce: workspace too small");
       }

@@ -99,6 +99,7 @@ void gemm_accumulate(Variable& v, const Tensor& A, bool ta, const Tensor& B, boo
   const void* pb = B.impl()->data();
   LMPB_OK_OR_THROW(lmpb_gemm_f32(ta, tb, static_cast<const float*>(pa), static_cast<const float*>(pb),
                                  static_cast<float*>(gi->storage->ptr), m, n, k, beta, tensor::current_stream()));
+  if (v.impl()->grad_hook) v.impl()->grad_hook();
 }
 
 }  // namespace

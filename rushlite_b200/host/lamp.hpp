@@ -233,6 +233,11 @@ struct VariableImpl {
   Tensor grad;
   bool requires_grad = false;
   std::shared_ptr<Function> grad_fn;
+  // Called during backward() right after a kernel that accumulates directly
+  // into this gradient's buffer (the matmul-gradient GEMM) has been queued on
+  // the backend stream; lets a data-parallel caller start that gradient's
+  // all-reduce while the rest of the backward is still running.
+  std::function<void()> grad_hook;
 };
 
 class Variable {

@@ -247,6 +247,19 @@ PYBIND11_MODULE(_C, m) {
       .def("numpy", [](const Variable& v, py::object out) { return to_numpy(v.data(), out); }, py::arg("out") = py::none())
       .def("zero_grad", &Variable::zero_grad)
       .def("realize", &Variable::realize)
+      .def("set_grad_hook", [](Variable& v, py::object fn) {
+             if (fn.is_none()) {
+               v.impl()->grad_hook = nullptr;
+               return;
+             }
+             auto f = std::make_shared<py::object>(fn);
+             v.impl()->grad_hook = [f]() {
+               py::gil_scoped_acquire gil;
+               (*f)();
+             };
+           }, py::arg("fn"),
+           "fn() runs during backward() as soon as a kernel writing this Variable's gradient "
+           "(the matmul-gradient GEMM) is queued; None removes it.")
       .def("__repr__", &repr_var)
       .def("__neg__", [](const Variable& a) { return aops::neg(a); })
       .def("__abs__", [](const Variable& a) { return aops::abs(a); })
