@@ -342,7 +342,7 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
   lmpb_status s = reduce_geometry(shape, ndim, axis, outer, R, inner);
   if (s != LMPB_OK) return s;
   if (outer * inner == 0) return LMPB_OK;
-  LMPB_CHECK_ARG(in && out, "lmpb_reduce: null pointer");
+  LMPB_CHECK_ARG(out && (in || R == 0), "lmpb_reduce: null pointer");  // an empty input may have no buffer
   cudaStream_t st = as_stream(stream);
   LMPB_DISPATCH_DTYPE(dtype, T, {
     ReducePlan p = plan_reduce<T>(in, out, outer, R, inner);
