@@ -155,9 +155,9 @@ lmpb_status lmpb_reduce(int op, int dtype, const void* in, const int64_t* shape,
  * call (a framework whose memory planner owns every allocation, a runtime
  * with a fixed device budget, a loop that cannot risk a pool miss turning
  * into cudaMalloc).  Same arguments and results as lmpb_reduce, but the
- * split-row workspace is a fixed 8 MiB scratch array inside the library,
+ * split-row workspace is a fixed 1 MiB scratch array inside the library,
  * held on every GPU that loads it until the process exits; nothing is
- * allocated or freed.  A reduction needing more than 8 MiB of scratch
+ * allocated or freed.  A reduction needing more than 1 MiB of scratch
  * (outer x inner x chunks x element size) returns LMPB_ERR_INVALID.
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture.  All calls share the one array:

@@ -142,51 +142,62 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-// Column reduction of [outer, R, inner]: thread owns VW adjacent columns of
-// one outer slice and rows [r0, r1) of chunk blockIdx.z; writes the partial
-// to dst[(chunk * outer + o) * inner + c].
+// Column reduction of [outer, R, inner].  A CTA is CTX column threads x CTY
+// row lanes: thread (tx, ty) owns VW adjacent columns and rows r0+ty,
+// r0+ty+CTY, ... of chunk blockIdx.z (4 rows in flight); the CTY lane
+// partials are folded in lane order through shared memory and the CTA's
+// partial goes to dst[(chunk * outer + o) * inner + c].  Narrow CTAs (CTX*VW
+// columns) fill the GPU with few row chunks, so the combine pass is small.
+constexpr int CTX = 16, CTY = kThreads / CTX;
+
 template <int OP, typename T, int VW>
 __global__ void __launch_bounds__(kThreads)
-    reduce_cols_kernel(const T* __restrict__ in, T* __restrict__ dst, int64_t outer, int64_t R,
-                       int64_t inner, int64_t rows_per_chunk) {
+    reduce_cols_kernel(const T* __restrict__ in, T* __restrict__ dst, int64_t outer, int64_t R, int64_t inner,
+                       int64_t rows_per_chunk) {
   using Rd = RedOp<OP, T>;
-  const int64_t cvec = (int64_t)blockIdx.x * kThreads + threadIdx.x;  // vector column index
-  const int64_t c = cvec * VW;
+  __shared__ T part[CTY][CTX * VW];
+  const int tx = threadIdx.x % CTX, ty = threadIdx.x / CTX;
+  const int64_t c = ((int64_t)blockIdx.x * CTX + tx) * VW;
   const int64_t o = blockIdx.y;
   const int64_t chunk = blockIdx.z;
-  if (c >= inner) return;
   const int64_t r0 = chunk * rows_per_chunk;
-  int64_t r1 = r0 + rows_per_chunk;
-  if (r1 > R) r1 = R;
-  const T* base = in + (o * R) * inner + c;
+  const int64_t r1 = min(R, r0 + rows_per_chunk);
   T acc[VW];
 #pragma unroll
   for (int j = 0; j < VW; ++j) acc[j] = Rd::identity();
-  if constexpr (VW > 1) {
-    int64_t r = r0;
-    // 8 rows of loads in flight per thread before the (in-order) accumulation
-    for (; r + 7 < r1; r += 8) {
-      V16<T> x[8];
+  if (c < inner) {
+    const T* base = in + (o * R) * inner + c;
+    int64_t r = r0 + ty;
+    if constexpr (VW > 1) {
+      for (; r + 3 * CTY < r1; r += 4 * CTY) {
+        V16<T> x[4];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u) * inner));
+        for (int u = 0; u < 4; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u * CTY) * inner));
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 4; ++u)
 #pragma unroll
-        for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
+          for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
+      }
+      for (; r < r1; r += CTY) {
+        V16<T> x;
+        x.raw = __ldg(reinterpret_cast<const uint4*>(base + r * inner));
+#pragma unroll
+        for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x.v[j]);
+      }
+    } else {
+      for (; r < r1; r += CTY) acc[0] = Rd::apply(acc[0], base[r * inner]);
     }
-    for (; r < r1; ++r) {
-      V16<T> x;
-      x.raw = __ldg(reinterpret_cast<const uint4*>(base + r * inner));
+  }
 #pragma unroll
-      for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x.v[j]);
+  for (int j = 0; j < VW; ++j) part[ty][tx * VW + j] = acc[j];
+  __syncthreads();
+  if (ty == 0 && c < inner) {
+#pragma unroll
+    for (int j = 0; j < VW; ++j) {
+      T v = part[0][tx * VW + j];
+      for (int k = 1; k < CTY; ++k) v = Rd::apply(v, part[k][tx * VW + j]);
+      dst[(chunk * outer + o) * inner + c + j] = v;
     }
-    V16<T> res;
-#pragma unroll
-    for (int j = 0; j < VW; ++j) res.v[j] = acc[j];
-    *reinterpret_cast<uint4*>(dst + (chunk * outer + o) * inner + c) = res.raw;
-  } else {
-    for (int64_t r = r0; r < r1; ++r) acc[0] = Rd::apply(acc[0], base[r * inner]);
-    dst[(chunk * outer + o) * inner + c] = acc[0];
   }
 }
 
@@ -236,7 +247,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 template <typename T>
 int64_t pick_chunks(int64_t outer, int64_t R, int64_t inner, int vw) {
-  const int64_t colblocks = (inner / vw + kThreads - 1) / kThreads;
+  const int64_t colblocks = (inner / vw + CTX - 1) / CTX;
   const int64_t ctas = colblocks * outer;
   const int64_t target = (int64_t)sm_count() * 8;
   if (ctas >= target || R < 64) return 1;
@@ -291,7 +302,7 @@ static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, c
     return launch_status("reduce_rows_kernel");
   }
   constexpr int N = V16<T>::N;
-  const int64_t colblocks = (p.inner / p.vw + kThreads - 1) / kThreads;
+  const int64_t colblocks = (p.inner / p.vw + CTX - 1) / CTX;
   const int64_t rows_per_chunk = (p.R + p.S - 1) / p.S;
   if (p.outer > 65535 || p.S > 65535)
     return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce: outer extent too large for the column kernel");

@@ -8,7 +8,7 @@
 // device budget, or a real-time loop that must not hit a pool miss that ends
 // in cudaMalloc).  This variant uses instead one fixed scratch array that
 // lives in the library's device data for as long as the library is loaded,
-// on every GPU that loads it (8 MiB each).
+// on every GPU that loads it (1 MiB each).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -26,10 +26,10 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
 
 namespace {
 
-// The split plan targets 8 CTAs per SM with 16-byte column vectors, so its
-// workspace is at most about 8 x SMs x 256 threads x 16 B (4.9 MB on a
-// 148-SM B200); 8 MiB covers it with margin.
-constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB per device
+// The split plan targets 8 CTAs per SM, each CTA 16 column threads of 16
+// bytes, so its workspace is at most about 8 x SMs x 256 B (0.3 MB on a
+// 148-SM B200); 1 MiB covers it with margin.
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
 
 // The scratch itself.  Host code must not pass `g_noalloc_scratch` to a
 // kernel: on the host the name is only a stand-in for the symbol, not a
