@@ -17,8 +17,7 @@
 //                 (A hi/lo, B hi/lo) into a STAGES-deep shared-memory ring,
 //                 64-byte swizzled, completion on an mbarrier;
 //      warp 1     owns two TMEM accumulators (128 lanes x BN fp32 columns
-//                 each; the epilogue drains one while the MMAs fill the
-//                 other) and
+//                 each: hi*hi and the cross terms) and
 //                 issues the tcgen05.mma.kind::tf32 instructions (one thread),
 //                 3 products x BK/8 MMAs per k-block, then tcgen05.commit
 //                 frees the stage;
@@ -54,7 +53,12 @@ constexpr int kThreads = 192;
 constexpr int A_TILE = BM * BK * 4;  // 8 KB
 constexpr int B_TILE = BN * BK * 4;  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
-constexpr int TMEM_COLS = 2 * BN;  // two accumulators: epilogue of tile i overlaps MMAs of tile i+1
+// Two accumulators per tile: hi*hi in columns [0, BN), the small cross terms
+// hi*lo + lo*hi in [BN, 2BN).  The tensor core's fp32 accumulation truncates,
+// so its error grows with the number of additions into one accumulator;
+// keeping the cross terms apart cuts the big accumulator's additions by 3x.
+// The epilogue adds the two with round-to-nearest.
+constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
 
@@ -225,8 +229,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;  // [2] accumulator ready for the epilogue
-  uint64_t* tempty = tfull + 2;      // [2] accumulator drained by the epilogue
+  uint64_t* tfull = empty + STAGES;  // accumulators ready for the epilogue
+  uint64_t* tempty = tfull + 2;      // accumulators drained by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -237,10 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(smem_u32(&tfull[a]), 1);
-      mbar_init(smem_u32(&tempty[a]), 128);  // every epilogue thread arrives
-    }
+    mbar_init(smem_u32(&tfull[0]), 1);
+    mbar_init(smem_u32(&tempty[0]), 128);  // every epilogue thread arrives
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
@@ -288,11 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int lt = 0;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++lt) {
-      const int acc = lt & 1;
-      const uint32_t aphase = (lt >> 1) & 1;
-      if (!mbar_wait(smem_u32(&tempty[acc]), aphase ^ 1, 4)) break;  // epilogue drained this accumulator
+      const uint32_t aphase = lt & 1;
+      if (!mbar_wait(smem_u32(&tempty[0]), aphase ^ 1, 4)) break;  // epilogue drained the accumulators
       tc_fence_after();
-      const uint32_t dtm = tmem + (uint32_t)(acc * BN);
+      const uint32_t dbig = tmem, dsmall = tmem + (uint32_t)BN;
       for (int kb = 0; kb < num_kb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t phase = (it / STAGES) & 1;
@@ -308,13 +309,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < BK / 8; ++kk) {
           const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
           const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-          mma_tf32(dtm, dAl + off, dBh + off, idesc, first);  // small terms first
-          mma_tf32(dtm, dAh + off, dBl + off, idesc, 1u);
-          mma_tf32(dtm, dAh + off, dBh + off, idesc, 1u);
+          mma_tf32(dsmall, dAl + off, dBh + off, idesc, first);
+          mma_tf32(dsmall, dAh + off, dBl + off, idesc, 1u);
+          mma_tf32(dbig, dAh + off, dBh + off, idesc, first);
         }
         mma_commit(smem_u32(&empty[s]));
       }
-      mma_commit(smem_u32(&tfull[acc]));
+      mma_commit(smem_u32(&tfull[0]));
     }
   } else if (warp >= 2) {
     // ---- epilogue: TMEM -> registers -> global, one tile behind the MMAs
@@ -322,18 +323,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool vec = (N & 3) == 0;
     int lt = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
-      const int acc = lt & 1;
-      const uint32_t aphase = (lt >> 1) & 1;
-      const bool ok = mbar_wait(smem_u32(&tfull[acc]), aphase, 3);
+      const uint32_t aphase = lt & 1;
+      const bool ok = mbar_wait(smem_u32(&tfull[0]), aphase, 3);
       tc_fence_after();
       int m0, n0;
       tile_coords(t, tiles_m, tiles_n, m0, n0);
       const int row = m0 + q * 32 + lane;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
+        uint32_t r[16], rs[16];
         tmem_ld16(taddr + c, r);
+        tmem_ld16(taddr + BN + c, rs);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(rs[j])));
         if (!ok || row >= M) continue;
         float* crow = C + (int64_t)row * N + n0 + c;
         const int ncols = min(16, N - (n0 + c));
@@ -361,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(smem_u32(&tempty[acc]));
+      mbar_arrive(smem_u32(&tempty[0]));
       if (!ok) break;
     }
   }

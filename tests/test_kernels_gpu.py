@@ -311,3 +311,19 @@ def test_fused_column_reduce(cuda, shape):
     want = port.binary(capi.CLAMP_BACKWARD, x, g, p0=0.0, p1=1.7976931348623157e308)
     assert_bitexact(host(out), want)
     assert rel_err(host(dbias), bias0.astype(np.float64) + want.astype(np.float64).sum(0)) <= 1e-5
+
+
+@pytest.mark.parametrize("mkn,tol", [((2048, 2048, 2048), 1e-5), ((4096, 4096, 4096), 1e-4),
+                                     ((32768, 4096, 512), 1e-4), ((4096, 1024, 4096), 1e-5)])
+def test_gemm_f32_c4_sizes(cuda, mkn, tol):
+    """BASELINE C4 tolerances: rel <= 1e-5, and <= 1e-4 at K >= 4096, against fp64."""
+    torch = cuda
+    m, k, n = mkn
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    A = torch.randn(m, k, device="cuda", generator=g) / k ** 0.5
+    B = torch.randn(k, n, device="cuda", generator=g) / k ** 0.5
+    C = torch.empty(m, n, device="cuda")
+    capi.gemm_f32(0, 0, A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, 0.0)
+    capi.device_error()
+    ref = A.double() @ B.double()
+    assert ((C.double() - ref).abs().max() / ref.abs().max()).item() <= tol
