@@ -242,19 +242,32 @@ def _time(torch, fn, iters, warmup=3):
     return e0.elapsed_time(e1) / iters
 
 
-def workload_c3(rsl, torch, args):
+def workload_c3(rsl, torch, args, rank=0, world=1):
     """Dim-wise reductions of fp32 N(0,1) and int32 U{-1000..1000} [16384, 4096], plus the
-    backward of sum (grad_a += broadcast of g).  GB/s = algorithmic bytes / event time."""
+    backward of sum (grad_a += broadcast of g).  GB/s = algorithmic bytes / event time.
+    On N ranks each rank owns a [16384, 4096] row block of a [16384*N, 4096] tensor (weak
+    scaling): dim-1 results stay local, dim-0 partials are combined with one all-reduce."""
+    from rushlite_b200 import distributed as D
+
     R, C = 16384, 4096
-    rng = np.random.default_rng(3)
+    rng = np.random.default_rng(3 + rank)
     xf = rsl.Variable(rng.standard_normal((R, C), dtype=np.float32), requires_grad=True)
     xi = rsl.Variable(rng.integers(-1000, 1001, (R, C)).astype(np.int32), dtype=rsl.dtype.int32)
     nbytes = R * C * 4
     res, tot_b, tot_ms = {}, 0, 0.0
+    ops = {"sum": "sum", "max": "max", "min": "min", "int32_sum": "sum"}
     for name, x, fn in [("sum", xf, rsl.sum), ("max", xf, rsl.max), ("min", xf, rsl.min), ("int32_sum", xi, rsl.sum)]:
         for axis in (0, 1):
             out_b = (C if axis == 0 else R) * 4
-            ms = _time(torch, lambda: fn(x, axis).realize(), args.steps)
+
+            def run(fn=fn, x=x, axis=axis, name=name):
+                r = fn(x, axis)
+                if axis == 0 and world > 1:
+                    D.all_reduce_(r.data, ops[name])  # the one exchange step
+                else:
+                    r.realize()
+
+            ms = D.max_over_ranks(_time(torch, run, args.steps))
             res[f"{name}_dim{axis}"] = {"ms": ms, "GB/s": (nbytes + out_b) / ms / 1e6}
             tot_b += nbytes + out_b
             tot_ms += ms
@@ -272,16 +285,20 @@ def workload_c3(rsl, torch, args):
         _backlog(torch)
         evs = [bw() for _ in range(args.steps)]
         torch.cuda.synchronize()
-        ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+        ms = D.max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
         res[f"sum_backward_dim{axis}"] = {"ms": ms, "GB/s": 2 * nbytes / ms / 1e6}
         tot_b += 2 * nbytes
         tot_ms += ms
     peak, src = peak_hbm()
-    value = tot_b / tot_ms / 1e6
+    value = tot_b / tot_ms / 1e6 * world
+    if world > 1:
+        for v in res.values():
+            v["GB/s"] *= world  # aggregate over ranks
     return {"metric": "dim-wise reduction HBM GB/s (C3, all ops)", "value": value, "unit": "GB/s",
+            "n_gpus": world, "scaling": "weak",
             "higher_is_better": True, "dtype": "f32/i32", "config": {"workload": "C3 reductions", "shape": [R, C]},
-            "ops": res, "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s",
-                                     "frac": value / peak, "peak_source": src}}
+            "ops": res, "roofline": {"bound": "hbm", "achieved": value / world, "peak": peak, "unit": "GB/s",
+                                     "frac": value / world / peak, "peak_source": src, "per": "GPU"}}
 
 
 def workload_c4(rsl, torch, args):
@@ -457,9 +474,11 @@ def main():
     if args.workload != "c2":
         if args.workload == "c5":
             line = workload_c5(rsl, torch, args, rank, world, pg)
+        elif args.workload == "c3":
+            line = workload_c3(rsl, torch, args, rank, world)
         elif rank == 0:
             l0 = rsl.cuda.kernel_launches()
-            line = {"c1": workload_c1, "c3": workload_c3, "c4": workload_c4}[args.workload](rsl, torch, args)
+            line = {"c1": workload_c1, "c4": workload_c4}[args.workload](rsl, torch, args)
             line["gpu_launches_total"] = int(rsl.cuda.kernel_launches() - l0)
         if rank == 0:
             line.setdefault("n_gpus", world)
