@@ -136,6 +136,29 @@ class Tensor {
 
 std::ostream& operator<<(std::ostream& os, const Tensor& t);
 
+// ---------------------------------------------------- asynchronous host I/O
+//
+// Host transfers on two per-device copy streams (one per direction), ordered
+// against the compute stream with events, so an upload or download overlaps
+// compute already queued and a download of one step overlaps the upload of
+// the next (PCIe is full duplex).  Host buffers should be pinned for the
+// copies to be asynchronous, and must stay valid until the copy completes.
+
+// A pending device-to-host copy; wait() blocks until the bytes are on the
+// host.  It keeps the source storage alive until then.
+struct HostCopy {
+  Storage keep;
+  void* done = nullptr;  // cudaEvent_t
+  void wait();
+  ~HostCopy();
+};
+
+// New CUDA tensor filled from `data` (same dtype, contiguous) on the upload
+// stream; compute queued after this call waits for the copy.
+Tensor upload_async(const void* data, const std::vector<size_t>& shape, DataType dtype);
+// Queue a copy of `t` (realized first) into `dst` (t's dtype, numel elements).
+std::shared_ptr<HostCopy> download_async(const Tensor& t, void* dst);
+
 // ------------------------------------------------------------ lazy capture
 namespace lazy {
 void set_capture_enabled(bool enabled);

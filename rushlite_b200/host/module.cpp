@@ -170,6 +170,19 @@ PYBIND11_MODULE(_C, m) {
   cuda.def("kernel_launches", []() { return lmpb_kernel_launches(); },
            "Kernels launched by the backend library so far in this process.");
 
+  py::class_<lmp::tensor::HostCopy, std::shared_ptr<lmp::tensor::HostCopy>>(m, "_HostCopy")
+      .def("wait", &lmp::tensor::HostCopy::wait, py::call_guard<py::gil_scoped_release>(),
+           "Block until the download has landed in host memory.");
+
+  // Asynchronous host I/O (additive): overlap PCIe transfers with compute.
+  m.def("upload", [](py::array arr, bool requires_grad) {
+        py::array a = py::array::ensure(arr, py::array::c_style);
+        std::vector<size_t> shape(a.shape(), a.shape() + a.ndim());
+        return Variable(lmp::tensor::upload_async(a.data(), shape, np_dtype(a.dtype())), requires_grad);
+      }, py::arg("array"), py::arg("requires_grad") = false,
+      "CUDA Variable with the array's dtype, copied on the upload stream; later ops wait for it. "
+      "Pass pinned memory for an asynchronous copy; keep the array alive and unchanged until then.");
+
   // ----------------------------------------------------------- _Tensor
   auto tcls = py::class_<Tensor>(m, "_Tensor")
       .def(py::init<const std::vector<double>&, const std::vector<size_t>&, DeviceType, DataType>(),
@@ -189,6 +202,12 @@ PYBIND11_MODULE(_C, m) {
       .def("realize", &Tensor::realize)
       .def("tolist", [](const Tensor& t) { return t.to_vector(); })
       .def("numpy", [](const Tensor& t, py::object out) { return to_numpy(t, out); }, py::arg("out") = py::none())
+      .def("download_async", [](const Tensor& t, py::array out) {
+             if (!(out.flags() & py::array::c_style) || (size_t)out.size() != t.numel() || np_dtype(out.dtype()) != t.type())
+               throw py::value_error("download_async: need a C-contiguous array of the tensor's dtype and size");
+             return lmp::tensor::download_async(t, out.mutable_data());
+           }, py::arg("out"), py::keep_alive<0, 2>(),
+           "Queue a copy into `out` on the download stream; returns a handle whose wait() blocks until it lands.")
       .def("data_ptr", [](Tensor& t) { return reinterpret_cast<uintptr_t>(t.data()); })
       // zero-copy view for other CUDA libraries (torch.as_tensor, NCCL through torch.distributed);
       // realizes the tensor; work on it is ordered on the backend's stream

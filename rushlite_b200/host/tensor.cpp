@@ -277,6 +277,90 @@ void Tensor::fill(Scalar item) {
 
 void Tensor::realize() { impl_->data(); }
 
+// ---------------------------------------------------- asynchronous host I/O
+
+namespace {
+struct CopyStreams {
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+};
+
+CopyStreams& copy_streams() {
+  static std::mutex mu;
+  static std::vector<CopyStreams> per_dev;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)per_dev.size() <= dev) per_dev.resize(dev + 1);
+  CopyStreams& c = per_dev[dev];
+  if (!c.h2d) {
+    // non-blocking: no implicit ordering with the legacy default stream
+    LMP_CHECK(cudaStreamCreateWithFlags(&c.h2d, cudaStreamNonBlocking) == cudaSuccess, "copy stream creation failed");
+    LMP_CHECK(cudaStreamCreateWithFlags(&c.d2h, cudaStreamNonBlocking) == cudaSuccess, "copy stream creation failed");
+  }
+  return c;
+}
+
+cudaEvent_t new_event() {
+  cudaEvent_t e;
+  LMP_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess, "cudaEventCreate failed");
+  return e;
+}
+
+void check_cuda(cudaError_t e, const char* what) { LMP_CHECK(e == cudaSuccess, what << ": " << cudaGetErrorString(e)); }
+}  // namespace
+
+void HostCopy::wait() {
+  if (!done) return;
+  check_cuda(cudaEventSynchronize(static_cast<cudaEvent_t>(done)), "download wait");
+  cudaEventDestroy(static_cast<cudaEvent_t>(done));
+  done = nullptr;
+  keep.reset();
+}
+
+HostCopy::~HostCopy() {
+  if (done) {
+    cudaEventSynchronize(static_cast<cudaEvent_t>(done));
+    cudaEventDestroy(static_cast<cudaEvent_t>(done));
+  }
+}
+
+Tensor upload_async(const void* data, const std::vector<size_t>& shape, DataType dtype) {
+  ImplPtr p = new_impl(shape, dtype, DeviceType::CUDA, true);
+  const size_t bytes = p->nbytes();
+  if (bytes == 0) return Tensor(p);
+  CopyStreams& cs = copy_streams();
+  cudaStream_t compute = static_cast<cudaStream_t>(g_stream);
+  cudaEvent_t ready = new_event(), copied = new_event();
+  // the allocation was ordered on the compute stream: let the copy start after it
+  check_cuda(cudaEventRecord(ready, compute), "upload: record");
+  check_cuda(cudaStreamWaitEvent(cs.h2d, ready, 0), "upload: wait");
+  check_cuda(cudaMemcpyAsync(p->storage->ptr, data, bytes, cudaMemcpyHostToDevice, cs.h2d), "upload: copy");
+  check_cuda(cudaEventRecord(copied, cs.h2d), "upload: record");
+  check_cuda(cudaStreamWaitEvent(compute, copied, 0), "upload: order");
+  cudaEventDestroy(ready);
+  cudaEventDestroy(copied);
+  return Tensor(p);
+}
+
+std::shared_ptr<HostCopy> download_async(const Tensor& t, void* dst) {
+  LMP_CHECK(t.device() == DeviceType::CUDA, "download_async: CUDA tensors only");
+  auto h = std::make_shared<HostCopy>();
+  const size_t bytes = t.impl()->nbytes();
+  void* src = t.impl()->data();
+  if (bytes == 0) return h;
+  CopyStreams& cs = copy_streams();
+  cudaEvent_t ready = new_event();
+  check_cuda(cudaEventRecord(ready, static_cast<cudaStream_t>(g_stream)), "download: record");
+  check_cuda(cudaStreamWaitEvent(cs.d2h, ready, 0), "download: wait");
+  check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, cs.d2h), "download: copy");
+  cudaEventDestroy(ready);
+  cudaEvent_t done = new_event();
+  check_cuda(cudaEventRecord(done, cs.d2h), "download: record");
+  h->done = done;
+  h->keep = t.impl()->storage;
+  return h;
+}
+
 std::ostream& operator<<(std::ostream& os, const Tensor& t) {
   os << "Tensor(dtype=" << dtype_name(t.type()) << ", device=" << (t.device() == DeviceType::CUDA ? "CUDA" : "CPU")
      << ", shape=[";

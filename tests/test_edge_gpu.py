@@ -114,3 +114,34 @@ def test_bias_grad_column_reduce(rsl):
     h.backward()
     want = ((x + bias) > 0).sum(0).astype(np.float64)
     assert rel_err(Bv.grad.numpy(), want) <= 1e-6
+
+
+def test_async_upload_download(rsl, cuda):
+    """rsl.upload / download_async on the copy streams: results equal the
+    synchronous path, across back-to-back steps that overlap."""
+    torch = cuda
+    rng = np.random.default_rng(11)
+    a = torch.empty((512, 1024), dtype=torch.float32, pin_memory=True).numpy()
+    b = torch.empty((512, 1), dtype=torch.float32, pin_memory=True).numpy()
+    a[...] = rng.random((512, 1024), dtype=np.float32)
+    b[...] = rng.random((512, 1), dtype=np.float32)
+    outs = [torch.empty((512, 1024), dtype=torch.float32, pin_memory=True).numpy() for _ in range(3)]
+    handles = []
+    for i in range(3):
+        A = rsl.upload(a, True)
+        B = rsl.upload(b)
+        with rsl.capture_on():
+            d = rsl.exp(A * B) - A
+        handles.append(d.data.download_async(outs[i]))
+        d.backward()
+        handles.append(None)
+    for h in handles:
+        if h is not None:
+            h.wait()
+    want = V(rsl, a) * V(rsl, b)
+    want = (rsl.exp(want) - V(rsl, a)).numpy()
+    for o in outs:
+        assert_bitexact(o, want)
+    g = np.zeros((512, 1024), np.float32)
+    A.grad.download_async(g).wait()
+    assert rel_err(g, np.exp(a.astype(np.float64) * b) * b - 1) <= 1e-5
