@@ -478,6 +478,9 @@ def main():
 
     rsl.cuda.set_device(local)
     if args.workload != "c2":
+        clocks = Clocks(local)
+        clocks.start()
+        wall0 = time.time()
         if args.workload == "c5":
             line = workload_c5(rsl, torch, args, rank, world, pg)
         elif args.workload == "c3":
@@ -486,7 +489,10 @@ def main():
             l0 = rsl.cuda.kernel_launches()
             line = {"c1": workload_c1, "c4": workload_c4}[args.workload](rsl, torch, args)
             line["gpu_launches_total"] = int(rsl.cuda.kernel_launches() - l0)
+        # the whole workload (warm-up included) is the sampled window here
+        clk = clocks.stop(wall0, time.time())
         if rank == 0:
+            line["clocks"] = clk
             line.setdefault("n_gpus", world)
             line["data"] = "synthetic (seeded)"
             print(json.dumps(line), flush=True)

@@ -169,33 +169,60 @@ __device__ __forceinline__ void split(float x, float& hi, float& lo) {
   lo = tf32_rne(__fsub_rn(x, hi));
 }
 
-// src is [rows, K] row-major: hi/lo [rows, Kp] with zero padding.
+// src is [rows, K] row-major, K == Kp: a flat float4 stream. Each CTA owns
+// 1024 consecutive float4s and each thread keeps four loads in flight.
 __global__ void __launch_bounds__(256)
-    split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
-                        float* __restrict__ hi, float* __restrict__ lo) {
-  const int64_t n = rows * Kp;
-  for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
-    const int64_t r = i / Kp, c = i - r * Kp;
-    float h = 0.f, l = 0.f;
-    if (c < K) split(src[r * K + c], h, l);
-    hi[i] = h;
-    lo[i] = l;
+    split_flat_kernel(const float4* __restrict__ src, int64_t n4, float4* __restrict__ hi, float4* __restrict__ lo) {
+  const int64_t base = (int64_t)blockIdx.x * 1024 + threadIdx.x;
+  float4 x[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (base + u * 256 < n4) x[u] = __ldg(src + base + u * 256);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int64_t i = base + u * 256;
+    if (i < n4) {
+      float4 h, l;
+      split(x[u].x, h.x, l.x);
+      split(x[u].y, h.y, l.y);
+      split(x[u].z, h.z, l.z);
+      split(x[u].w, h.w, l.w);
+      hi[i] = h;
+      lo[i] = l;
+    }
   }
 }
 
+// src is [rows, K] row-major, K < Kp: one CTA row-walk per row, zero padding.
+__global__ void __launch_bounds__(256)
+    split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
+                        float* __restrict__ hi, float* __restrict__ lo) {
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
+    for (int64_t c = threadIdx.x; c < Kp; c += 256) {
+      float h = 0.f, l = 0.f;
+      if (c < K) split(src[r * K + c], h, l);
+      hi[r * Kp + c] = h;
+      lo[r * Kp + c] = l;
+    }
+}
+
 // src is [K, rows] row-major (the operand transposed): hi/lo [rows, Kp].
+// 64 x 64 tiles through shared memory, 16 elements per thread, both the
+// read (along rows) and the writes (along K) coalesced.
 __global__ void __launch_bounds__(256)
     split_transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
                            float* __restrict__ hi, float* __restrict__ lo) {
-  __shared__ float tile[32][33];
-  const int64_t k0 = (int64_t)blockIdx.y * 32, r0 = (int64_t)blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int j = ty; j < 32; j += 8) {
+  __shared__ float tile[64][65];
+  const int64_t k0 = (int64_t)blockIdx.y * 64, r0 = (int64_t)blockIdx.x * 64;
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+#pragma unroll
+  for (int j = ty; j < 64; j += 4) {
     const int64_t k = k0 + j, r = r0 + tx;
-    tile[j][tx] = (k < K && r < rows) ? src[k * rows + r] : 0.f;
+    tile[j][tx] = (k < K && r < rows) ? __ldg(src + k * rows + r) : 0.f;
   }
   __syncthreads();
-  for (int j = ty; j < 32; j += 8) {
+#pragma unroll
+  for (int j = ty; j < 64; j += 4) {
     const int64_t r = r0 + j, k = k0 + tx;
     if (r < rows && k < Kp) {
       float h, l;
@@ -411,14 +438,19 @@ lmpb_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t 
 
 lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K, int64_t Kp, float* hi,
                           float* lo, cudaStream_t st) {
-  if (kmajor) {
-    const int64_t n = rows * Kp;
-    int64_t blocks = (n + 255) / 256;
-    if (blocks > (int64_t)sm_count() * 16) blocks = (int64_t)sm_count() * 16;
-    split_kmajor_kernel<<<(int)blocks, 256, 0, st>>>(src, rows, K, Kp, hi, lo);
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (kmajor && K == Kp && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+    const int64_t n4 = rows * K / 4;  // K is a multiple of BK, so of 4
+    const int64_t blocks = (n4 + 1023) / 1024;
+    if (blocks > INT32_MAX) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: operand too large for the split pass");
+    split_flat_kernel<<<(unsigned)std::max<int64_t>(1, blocks), 256, 0, st>>>(
+        reinterpret_cast<const float4*>(src), n4, reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
+  } else if (kmajor) {
+    split_kmajor_kernel<<<(int)std::max<int64_t>(1, std::min<int64_t>(rows, cap)), 256, 0, st>>>(src, rows, K, Kp,
+                                                                                               hi, lo);
   } else {
-    if ((Kp + 31) / 32 > 65535) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
-    dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((Kp + 31) / 32));
+    if ((Kp + 63) / 64 > 65535) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
+    dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64));
     split_transpose_kernel<<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo);
   }
   return launch_status("gemm split pass");
