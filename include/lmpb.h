@@ -170,13 +170,15 @@ lmpb_status lmpb_reduce_noalloc(int op, int dtype, const void* in, const int64_t
 
 /* C[m,n] = A[m,k] · B[k,n], row-major, converted to out_dtype
  * (matmul_cuda, csrc/src/tensor/cuda/kernels.cu:83-110; cuda/matrix.cu:178-199).
- * fp32 × fp32 → fp32 runs on the tcgen05 tensor cores as 3xTF32 (hi·hi + hi·lo
- * + lo·hi, fp32 accumulate in TMEM); other dtype combinations use a SIMT
- * kernel that accumulates in out_dtype like the reference. */
+ * fp32 × fp32 → fp32 runs on the tcgen05 tensor cores: every row of A and
+ * column of B is scaled by a power of two into fp16 range and split into
+ * fp16 hi and lo parts, and hi·hi + hi·lo + lo·hi accumulate in fp32 in TMEM
+ * (fp32-level accuracy, Inf/NaN propagate); other dtype combinations use a
+ * SIMT kernel that accumulates in out_dtype like the reference. */
 lmpb_status lmpb_matmul(int out_dtype, const void* A, int a_dtype, const void* B, int b_dtype,
                         void* C, int64_t m, int64_t k, int64_t n, void* stream);
 
-/* fp32 GEMM with operand transposes and accumulate, on the same 3xTF32
+/* fp32 GEMM with operand transposes and accumulate, on the same
  * tensor-core path:  C[m,n] = op(A)·op(B) + beta·C, op(X) = X or Xᵀ of a
  * row-major array (A is [m,k] or, with trans_a, [k,m]; B is [k,n] or, with
  * trans_b, [n,k]).  beta is 0 or 1.  This lets autograd compute

@@ -1,16 +1,28 @@
-// fp32 GEMM on the B200 tensor cores: 3xTF32 with tcgen05, TMEM and TMA.
+// fp32 GEMM on the B200 tensor cores: three fp16 products per operand pair
+// (tcgen05.mma kind::f16, fp32 accumulation in TMEM), TMA-fed.
 //
 //   C[m,n] = op(A)[m,k] · op(B)[k,n] (+ C when beta = 1), fp32 in and out.
 //
-// fp32 accuracy is kept by splitting every operand element x into
-// hi = tf32(x) and lo = tf32(x - hi) (round to nearest) and accumulating
-// hi·hi + hi·lo + lo·hi in fp32 in TMEM; the dropped lo·lo term and the tf32
-// rounding of lo are O(2^-22) relative, below fp32 accumulation error.
+// fp32 accuracy from fp16 tensor cores (the split of Ootomo & Yokota, 2022,
+// "Recovering single precision accuracy from Tensor Cores while surpassing
+// the FP32 theoretical peak performance", with a power-of-two scale per row):
+// every row r of op(A) (and every column of op(B)) is scaled by 2^e_r so its
+// largest finite magnitude lies in [2^14, 2^15); each scaled element x becomes
+//     hi = fp16(x),  lo = fp16((x - hi) * 2^11)        (round to nearest)
+// and the tile accumulates big = hi·hi and small = hi·lo + lo·hi in two fp32
+// TMEM accumulators; the epilogue forms (big + small * 2^-11) * 2^-(e_r+e_c).
+// hi and lo each carry 11 significant bits, as tf32 would, but kind::f16
+// runs at twice the kind::tf32 rate.  The dropped lo·lo term is 2^-22
+// relative.  Scales are exact powers of two; a scaled element below
+// 2^-13 (2^-27 of its row's maximum) loses bits of lo to fp16 subnormals,
+// an absolute error under 2^-40 of the row's largest product.  Inf and NaN
+// pass through: the scale ignores non-finite values and lo is 0 where hi is inf.
 //
-// 1. A split pass writes hi and lo planes of both operands, K-major (rows of
-//    K contiguous fp32, K padded to the k-block), transposing op(A) / op(B)
-//    on the way when the caller's layout is not K-major.  It reads each input
-//    element once and writes 8 bytes; for 4096^3 that is ~1.5% of the GEMM.
+// 1. A split pass per operand: the row maxima (a column-max kernel when the
+//    operand must be transposed), then hi/lo fp16 planes, K-major (rows of K
+//    contiguous, K padded to the k-block), transposing when the caller's
+//    layout is not K-major.  It reads each input element twice (the second
+//    read mostly from L2) and writes 4 bytes.
 // 2. The GEMM kernel: persistent, one CTA per SM walking 128 x BN output
 //    tiles in grouped order, 6 warps:
 //      warp 0     TMA producer (one elected thread): 4 tiles per k-block
@@ -18,18 +30,19 @@
 //                 64-byte swizzled, completion on an mbarrier;
 //      warp 1     owns two TMEM accumulators (128 lanes x BN fp32 columns
 //                 each: hi*hi and the cross terms) and
-//                 issues the tcgen05.mma.kind::tf32 instructions (one thread),
-//                 3 products x BK/8 MMAs per k-block, then tcgen05.commit
+//                 issues the tcgen05.mma.kind::f16 instructions (one thread),
+//                 3 products x BK/16 MMAs per k-block, then tcgen05.commit
 //                 frees the stage;
 //      warps 2-5  epilogue: tcgen05.ld 32x32b from TMEM (each warp reads the
-//                 32 lanes its rank in the warpgroup may access), optional
-//                 + C, 16-byte stores.
+//                 32 lanes its rank in the warpgroup may access), combine and
+//                 unscale, optional + C, 16-byte stores.
 //    Every mbarrier wait is bounded (clock64); on expiry the kernel records
 //    an error code in a device word, stops issuing, frees TMEM and returns.
 //    No cluster launch and no multicast: each CTA loads its own tiles.
 // Shapes that TMA cannot describe or that are too small for a 128-row tile
 // use the SIMT kernel (gemm_simt.cu).
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -47,17 +60,16 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int BK = 16;      // 16 fp32 = 64 bytes per row = one 64B swizzle atom
+constexpr int BK = 32;      // 32 fp16 = 64 bytes per row = one 64B swizzle atom
 constexpr int STAGES = 4;
 constexpr int kThreads = 192;
-constexpr int A_TILE = BM * BK * 4;  // 8 KB
-constexpr int B_TILE = BN * BK * 4;  // 16 KB
+constexpr int A_TILE = BM * BK * 2;  // 8 KB
+constexpr int B_TILE = BN * BK * 2;  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
-// Two accumulators per tile: hi*hi in columns [0, BN), the small cross terms
-// hi*lo + lo*hi in [BN, 2BN).  The tensor core's fp32 accumulation truncates,
-// so its error grows with the number of additions into one accumulator;
-// keeping the cross terms apart cuts the big accumulator's additions by 3x.
-// The epilogue adds the two with round-to-nearest.
+// Two accumulators per tile: hi*hi in columns [0, BN), the cross terms
+// hi*lo + lo*hi (scaled by 2^11) in [BN, 2BN).  Keeping them apart also keeps
+// the tensor core's truncating fp32 accumulation to one product per add in
+// the big accumulator.
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
@@ -124,14 +136,15 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 
-// kind::tf32 instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=BN.
+// kind::f16 instruction descriptor: D f32, A and B both f16 (format 0), both
+// K-major, M=128, N=BN.
 __host__ __device__ constexpr uint32_t instr_desc() {
-  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n"
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
       ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
@@ -154,81 +167,144 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 
 // ------------------------------------------------------------ split pass
 
-// Round to the nearest tf32 value (10 explicit mantissa bits), ties to even.
-__device__ __forceinline__ float tf32_rne(float x) {
-  uint32_t u = __float_as_uint(x);
-  if ((u & 0x7F800000u) != 0x7F800000u) {  // finite
-    u += 0x0FFFu + ((u >> 13) & 1u);
-    u &= 0xFFFFE000u;
-  }
-  return __uint_as_float(u);
+// |x| for finite x, else 0: row scales ignore Inf and NaN.
+__device__ __forceinline__ float finite_abs(float x) {
+  const float a = fabsf(x);
+  return a < INFINITY ? a : 0.f;
 }
 
-__device__ __forceinline__ void split(float x, float& hi, float& lo) {
-  hi = tf32_rne(x);
-  lo = tf32_rne(__fsub_rn(x, hi));
+// e such that mx * 2^e lies in [2^14, 2^15); 0 for a row without finite
+// non-zero values.
+__host__ __device__ __forceinline__ int row_exp(float mx) {
+  if (!(mx > 0.f) || !(mx < INFINITY)) return 0;
+  int p;
+  frexpf(mx, &p);  // mx = f * 2^p, f in [0.5, 1)
+  return 15 - p;
 }
 
-// src is [rows, K] row-major, K == Kp: a flat float4 stream. Each CTA owns
-// 1024 consecutive float4s and each thread keeps four loads in flight.
+// x * 2^e, exact (up to one rounding when the result is subnormal).
+__device__ __forceinline__ float pow2_scale(float x, int e) {
+  if (e >= -126 && e <= 127) return x * __int_as_float((e + 127) << 23);
+  return ldexpf(x, e);
+}
+
+// Scaled element -> (hi, lo): hi = fp16(xs), lo = fp16((xs - hi) * 2^11).
+__device__ __forceinline__ void split16(float xs, __half& hi, __half& lo) {
+  hi = __float2half_rn(xs);
+  const float h = __half2float(hi);
+  lo = __hisinf(hi) ? __float2half_rn(0.f) : __float2half_rn(__fsub_rn(xs, h) * 2048.f);
+}
+
+__device__ __forceinline__ float block_max256(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();  // red is reused by the next row
+  return m;
+}
+
+// src is [rows, K] row-major (K-major already).  One CTA per row at a time:
+// the row's finite max-abs, then hi/lo [rows, Kp] with zero padding; rowmax
+// receives the max for the epilogue.  vec: K % 4 == 0 and src 16-byte aligned.
+template <bool vec>
 __global__ void __launch_bounds__(256)
-    split_flat_kernel(const float4* __restrict__ src, int64_t n4, float4* __restrict__ hi, float4* __restrict__ lo) {
-  const int64_t base = (int64_t)blockIdx.x * 1024 + threadIdx.x;
-  float4 x[4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u)
-    if (base + u * 256 < n4) x[u] = __ldg(src + base + u * 256);
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int64_t i = base + u * 256;
-    if (i < n4) {
-      float4 h, l;
-      split(x[u].x, h.x, l.x);
-      split(x[u].y, h.y, l.y);
-      split(x[u].z, h.z, l.z);
-      split(x[u].w, h.w, l.w);
-      hi[i] = h;
-      lo[i] = l;
+    split_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp, __half* __restrict__ hi,
+                      __half* __restrict__ lo, float* __restrict__ rowmax) {
+  __shared__ float red[8];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* row = src + r * K;
+    float mx = 0.f;
+    if (vec) {
+      const float4* row4 = reinterpret_cast<const float4*>(row);
+      for (int64_t c = threadIdx.x; c < K / 4; c += 256) {
+        const float4 v = __ldg(row4 + c);
+        mx = fmaxf(fmaxf(mx, fmaxf(finite_abs(v.x), finite_abs(v.y))), fmaxf(finite_abs(v.z), finite_abs(v.w)));
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < K; c += 256) mx = fmaxf(mx, finite_abs(__ldg(row + c)));
+    }
+    mx = block_max256(mx, red);
+    if (threadIdx.x == 0) rowmax[r] = mx;
+    const int e = row_exp(mx);
+    __half* hrow = hi + r * Kp;
+    __half* lrow = lo + r * Kp;
+    if (vec) {  // Kp % 4 == 0; 4 halves = 8 bytes per store
+      const float4* row4 = reinterpret_cast<const float4*>(row);
+      for (int64_t c = threadIdx.x; c < Kp / 4; c += 256) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c * 4 < K) v = __ldg(row4 + c);
+        __half h[4], l[4];
+        split16(pow2_scale(v.x, e), h[0], l[0]);
+        split16(pow2_scale(v.y, e), h[1], l[1]);
+        split16(pow2_scale(v.z, e), h[2], l[2]);
+        split16(pow2_scale(v.w, e), h[3], l[3]);
+        *reinterpret_cast<uint2*>(hrow + c * 4) = *reinterpret_cast<const uint2*>(h);
+        *reinterpret_cast<uint2*>(lrow + c * 4) = *reinterpret_cast<const uint2*>(l);
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < Kp; c += 256) {
+        __half h = __float2half_rn(0.f), l = h;
+        if (c < K) split16(pow2_scale(row[c], e), h, l);
+        hrow[c] = h;
+        lrow[c] = l;
+      }
     }
   }
 }
 
-// src is [rows, K] row-major, K < Kp: one CTA row-walk per row, zero padding.
+// src is [K, rows] row-major (the operand transposed): the finite max-abs of
+// every column r over K, as float bits into colmax[r] (zeroed beforehand;
+// non-negative floats order like their bits).  CTA = 64 columns x 256 k.
 __global__ void __launch_bounds__(256)
-    split_kmajor_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
-                        float* __restrict__ hi, float* __restrict__ lo) {
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x)
-    for (int64_t c = threadIdx.x; c < Kp; c += 256) {
-      float h = 0.f, l = 0.f;
-      if (c < K) split(src[r * K + c], h, l);
-      hi[r * Kp + c] = h;
-      lo[r * Kp + c] = l;
-    }
+    colmax_kernel(const float* __restrict__ src, int64_t rows, int64_t K, unsigned* __restrict__ colmax) {
+  __shared__ float part[4][64];
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const int64_t r = (int64_t)blockIdx.x * 64 + tx;
+  const int64_t k0 = (int64_t)blockIdx.y * 256, k1 = k0 + 256 < K ? k0 + 256 : K;
+  float mx = 0.f;
+  if (r < rows)
+    for (int64_t k = k0 + ty; k < k1; k += 4) mx = fmaxf(mx, finite_abs(__ldg(src + k * rows + r)));
+  part[ty][tx] = mx;
+  __syncthreads();
+  if (ty == 0 && r < rows) {
+    mx = fmaxf(fmaxf(part[0][tx], part[1][tx]), fmaxf(part[2][tx], part[3][tx]));
+    if (mx > 0.f) atomicMax(colmax + r, __float_as_uint(mx));
+  }
 }
 
-// src is [K, rows] row-major (the operand transposed): hi/lo [rows, Kp].
-// 64 x 64 tiles through shared memory, 16 elements per thread, both the
-// read (along rows) and the writes (along K) coalesced.
+// src is [K, rows] row-major: hi/lo [rows, Kp] through 64 x 64 shared-memory
+// tiles, scaled by the column maxima; reads along rows and half2 writes along
+// K both coalesced.
 __global__ void __launch_bounds__(256)
     split_transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
-                           float* __restrict__ hi, float* __restrict__ lo) {
+                           const float* __restrict__ colmax, __half* __restrict__ hi, __half* __restrict__ lo) {
   __shared__ float tile[64][65];
   const int64_t k0 = (int64_t)blockIdx.y * 64, r0 = (int64_t)blockIdx.x * 64;
-  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+  {
+    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
 #pragma unroll
-  for (int j = ty; j < 64; j += 4) {
-    const int64_t k = k0 + j, r = r0 + tx;
-    tile[j][tx] = (k < K && r < rows) ? __ldg(src + k * rows + r) : 0.f;
+    for (int j = ty; j < 64; j += 4) {
+      const int64_t k = k0 + j, r = r0 + tx;
+      tile[j][tx] = (k < K && r < rows) ? __ldg(src + k * rows + r) : 0.f;
+    }
   }
   __syncthreads();
+  const int kx = threadIdx.x & 31, ry = threadIdx.x >> 5;  // 32 k-pairs x 8 rows
+  const int64_t k = k0 + 2 * kx;
 #pragma unroll
-  for (int j = ty; j < 64; j += 4) {
-    const int64_t r = r0 + j, k = k0 + tx;
-    if (r < rows && k < Kp) {
-      float h, l;
-      split(tile[tx][j], h, l);
-      hi[r * Kp + k] = h;
-      lo[r * Kp + k] = l;
+  for (int j = ry; j < 64; j += 8) {
+    const int64_t r = r0 + j;
+    if (r < rows && k < Kp) {  // Kp is even, so k + 1 < Kp too
+      const int e = row_exp(__ldg(colmax + r));
+      __half h0, h1, l0, l1;
+      split16(pow2_scale(tile[2 * kx][j], e), h0, l0);
+      split16(pow2_scale(tile[2 * kx + 1][j], e), h1, l1);
+      *reinterpret_cast<__half2*>(hi + r * Kp + k) = __halves2half2(h0, h1);
+      *reinterpret_cast<__half2*>(lo + r * Kp + k) = __halves2half2(l0, l1);
     }
   }
 }
@@ -249,9 +325,10 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 // Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
-                       const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                       float* __restrict__ C, int M, int N, int num_kb, int beta, int tiles_m, int tiles_n) {
+    gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
+                      const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
+                      const float* __restrict__ maxA, const float* __restrict__ maxB, float* __restrict__ C, int M,
+                      int N, int num_kb, int beta, int tiles_m, int tiles_n) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -333,12 +410,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_TILE);
         const uint64_t dBh = smem_desc(base + 2 * A_TILE), dBl = smem_desc(base + 2 * A_TILE + B_TILE);
 #pragma unroll
-        for (int kk = 0; kk < BK / 8; ++kk) {
-          const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 16 fp16 = 32 bytes along the swizzled row
           const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-          mma_tf32(dsmall, dAl + off, dBh + off, idesc, first);
-          mma_tf32(dsmall, dAh + off, dBl + off, idesc, 1u);
-          mma_tf32(dbig, dAh + off, dBh + off, idesc, first);
+          mma_f16(dsmall, dAl + off, dBh + off, idesc, first);
+          mma_f16(dsmall, dAh + off, dBl + off, idesc, 1u);
+          mma_f16(dbig, dAh + off, dBh + off, idesc, first);
         }
         mma_commit(smem_u32(&empty[s]));
       }
@@ -356,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m0, n0;
       tile_coords(t, tiles_m, tiles_n, m0, n0);
       const int row = m0 + q * 32 + lane;
+      const int erow = row < M ? row_exp(__ldg(maxA + row)) : 0;
       const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
@@ -363,11 +441,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld16(taddr + c, r);
         tmem_ld16(taddr + BN + c, rs);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(rs[j])));
+        for (int j = 0; j < 16; ++j) {
+          // an infinite hi*hi sum stands: its cross terms may hold inf*0 = NaN
+          const float big = __uint_as_float(r[j]);
+          r[j] = __float_as_uint(isinf(big) ? big : __fmaf_rn(__uint_as_float(rs[j]), 0x1p-11f, big));
+        }
         if (!ok || row >= M) continue;
         float* crow = C + (int64_t)row * N + n0 + c;
         const int ncols = min(16, N - (n0 + c));
         if (ncols <= 0) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = min(n0 + c + j, N - 1);
+          r[j] = __float_as_uint(pow2_scale(__uint_as_float(r[j]), -(erow + row_exp(__ldg(maxB + col)))));
+        }
         if (vec && ncols == 16) {
 #pragma unroll
           for (int j = 0; j < 16; j += 4) {
@@ -421,39 +508,43 @@ EncodeTiled encode_fn() {
   return fn;
 }
 
-// Tensor map over a [rows, Kp] fp32 plane, box = box_rows x BK, 128B swizzle.
-lmpb_status make_map(CUtensorMap* map, const float* base, int64_t rows, int64_t Kp, int box_rows) {
+// Tensor map over a [rows, Kp] fp16 plane, box = box_rows x BK, 64B swizzle.
+lmpb_status make_map(CUtensorMap* map, const __half* base, int64_t rows, int64_t Kp, int box_rows) {
   EncodeTiled enc = encode_fn();
   if (!enc) return set_error(LMPB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t dims[2] = {(cuuint64_t)Kp, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)Kp * 4};
+  cuuint64_t strides[1] = {(cuuint64_t)Kp * 2};
   cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(LMPB_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return LMPB_OK;
 }
 
-lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K, int64_t Kp, float* hi,
-                          float* lo, cudaStream_t st) {
-  const int64_t cap = (int64_t)sm_count() * 8;
-  if (kmajor && K == Kp && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
-    const int64_t n4 = rows * K / 4;  // K is a multiple of BK, so of 4
-    const int64_t blocks = (n4 + 1023) / 1024;
-    if (blocks > INT32_MAX) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: operand too large for the split pass");
-    split_flat_kernel<<<(unsigned)std::max<int64_t>(1, blocks), 256, 0, st>>>(
-        reinterpret_cast<const float4*>(src), n4, reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lo));
-  } else if (kmajor) {
-    split_kmajor_kernel<<<(int)std::max<int64_t>(1, std::min<int64_t>(rows, cap)), 256, 0, st>>>(src, rows, K, Kp,
-                                                                                               hi, lo);
-  } else {
-    if ((Kp + 63) / 64 > 65535) return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
-    dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64));
-    split_transpose_kernel<<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo);
+// One operand -> scaled fp16 hi/lo planes [rows, Kp] and its row maxima.
+// kmajor: src is [rows, K]; else src is [K, rows].  rowmax must be zeroed
+// beforehand when !kmajor.
+lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K, int64_t Kp, __half* hi,
+                          __half* lo, float* rowmax, cudaStream_t st) {
+  if (kmajor) {
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)sm_count() * 8));
+    if ((K & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0)
+      split_rows_kernel<true><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax);
+    else
+      split_rows_kernel<false><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax);
+    return launch_status("gemm split pass (rows)");
   }
-  return launch_status("gemm split pass");
+  if ((Kp + 63) / 64 > 65535 || (K + 255) / 256 > 65535)
+    return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
+  colmax_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + 255) / 256)), 256, 0, st>>>(
+      src, rows, K, reinterpret_cast<unsigned*>(rowmax));
+  lmpb_status s = launch_status("gemm split pass (column maxima)");
+  if (s != LMPB_OK) return s;
+  split_transpose_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64)), 256, 0, st>>>(
+      src, rows, K, Kp, rowmax, hi, lo);
+  return launch_status("gemm split pass (transpose)");
 }
 
 }  // namespace
@@ -467,21 +558,31 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attr_err = cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(attr_err));
   const int64_t Kp = (k + BK - 1) / BK * BK;
-  const size_t plane_a = (size_t)m * Kp * 4, plane_b = (size_t)n * Kp * 4;
-  void* ws = nullptr;
-  LMPB_CUDA_TRY(stream_alloc((void**)&ws, 2 * plane_a + 2 * plane_b, st));
-  float* Ah = static_cast<float*>(ws);
-  float* Al = reinterpret_cast<float*>(static_cast<char*>(ws) + plane_a);
-  float* Bh = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * plane_a);
-  float* Bl = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * plane_a + plane_b);
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t plane_a = up((size_t)m * Kp * 2), plane_b = up((size_t)n * Kp * 2);
+  const size_t max_a = up((size_t)m * 4), max_b = up((size_t)n * 4);
+  char* ws = nullptr;
+  LMPB_CUDA_TRY(stream_alloc((void**)&ws, 2 * plane_a + 2 * plane_b + max_a + max_b, st));
+  __half* Ah = reinterpret_cast<__half*>(ws);
+  __half* Al = reinterpret_cast<__half*>(ws + plane_a);
+  __half* Bh = reinterpret_cast<__half*>(ws + 2 * plane_a);
+  __half* Bl = reinterpret_cast<__half*>(ws + 2 * plane_a + plane_b);
+  float* mxA = reinterpret_cast<float*>(ws + 2 * plane_a + 2 * plane_b);
+  float* mxB = reinterpret_cast<float*>(ws + 2 * plane_a + 2 * plane_b + max_a);
   // op(A) is [m,k]: K-major as stored unless transposed; the MMA's B operand
   // is op(B)^T = [n,k]: K-major as stored only when trans_b.
-  lmpb_status s = split_operand(A, !trans_a, m, k, Kp, Ah, Al, st);
-  if (s == LMPB_OK) s = split_operand(B, trans_b != 0, n, k, Kp, Bh, Bl, st);
+  const bool ka = !trans_a, kb = trans_b != 0;
+  lmpb_status s = LMPB_OK;
+  if (!ka || !kb) {  // column maxima accumulate by atomicMax from zero
+    const cudaError_t e = cudaMemsetAsync(ws + 2 * plane_a + 2 * plane_b, 0, max_a + max_b, st);
+    if (e != cudaSuccess) s = set_error(LMPB_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  }
+  if (s == LMPB_OK) s = split_operand(A, ka, m, k, Kp, Ah, Al, mxA, st);
+  if (s == LMPB_OK) s = split_operand(B, kb, n, k, Kp, Bh, Bl, mxB, st);
   CUtensorMap mAh, mAl, mBh, mBl;
   if (s == LMPB_OK) s = make_map(&mAh, Ah, m, Kp, BM);
   if (s == LMPB_OK) s = make_map(&mAl, Al, m, Kp, BM);
@@ -494,10 +595,10 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
     } else {
       const int64_t ntiles = tiles_m * tiles_n;
       const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
-      gemm_3xtf32_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, C, (int)m, (int)n,
-                                                             (int)(Kp / BK), beta != 0.f ? 1 : 0, (int)tiles_m,
-                                                             (int)tiles_n);
-      s = launch_status("gemm_3xtf32_kernel");
+      gemm_f16x3_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, mxA, mxB, C, (int)m, (int)n,
+                                                            (int)(Kp / BK), beta != 0.f ? 1 : 0, (int)tiles_m,
+                                                            (int)tiles_n);
+      s = launch_status("gemm_f16x3_kernel");
     }
   }
   cudaError_t e = cudaFreeAsync(ws, st);

@@ -1,4 +1,4 @@
-// Matmul entry points.  fp32 x fp32 -> fp32 goes to the tcgen05 3xTF32 GEMM
+// Matmul entry points.  fp32 x fp32 -> fp32 goes to the tcgen05 split-fp16 GEMM
 // (gemm_sm100.cu); every other dtype combination runs the SIMT kernel here,
 // which accumulates in the output dtype over k in order, like the
 // reference's cpuMatmulKernel (csrc/src/tensor/cpu/matrix.cpp:8-19).

@@ -208,6 +208,53 @@ def test_gemm_f32(cuda, mkn, trans):
     assert rel_err(host(dC), want) <= 1e-5
 
 
+@pytest.mark.parametrize("trans", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_f32_wide_range(cuda, trans):
+    """Rows of A and columns of B spread over 2^-100 .. 2^50 (the tensor-core
+    path scales every row into fp16 range): each element within 1e-5 of
+    |A|·|B|, underflowing products to fp32's subnormal resolution."""
+    m, k, n = 256, 200, 384  # k pads to the k-block
+    rng = np.random.default_rng(7)
+    Am = rng.standard_normal((m, k)) * np.exp2(rng.integers(-100, 50, (m, 1)))
+    Bm = rng.standard_normal((k, n)) * np.exp2(rng.integers(-60, 60, (1, n)))
+    Am, Bm = Am.astype(np.float32), Bm.astype(np.float32)
+    A = np.ascontiguousarray(Am.T) if trans[0] else Am
+    B = np.ascontiguousarray(Bm.T) if trans[1] else Bm
+    want = Am.astype(np.float64) @ Bm.astype(np.float64)
+    bound = np.abs(Am.astype(np.float64)) @ np.abs(Bm.astype(np.float64))
+    dA, dB, dC = dev(cuda, A), dev(cuda, B), dev(cuda, np.zeros((m, n), np.float32))
+    capi.gemm_f32(trans[0], trans[1], dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), m, n, k, 0.0)
+    capi.device_error()
+    err = np.abs(host(dC).astype(np.float64) - want)
+    assert np.all(err <= 1e-5 * bound + 3e-45), float(np.max(err / (bound + 1e-300)))
+
+
+def test_gemm_f32_nonfinite(cuda):
+    """Inf and NaN in A propagate as in an fp32 dot product; the other
+    elements of those rows keep full accuracy (B is integer-valued, so its
+    low parts are exactly zero)."""
+    m, k, n = 256, 256, 256
+    rng = np.random.default_rng(8)
+    A = rng.standard_normal((m, k)).astype(np.float32)
+    A[3, 5] = np.inf
+    A[9, 0] = -np.inf
+    A[9, 1] = np.inf  # inf - inf = NaN wherever both B entries are non-zero
+    A[17, 100] = np.nan
+    A[40, :] = 0.0
+    B = rng.integers(1, 9, (k, n)).astype(np.float32)
+    B[5, 7] = 0.0  # inf * 0 = NaN in row 3, column 7
+    with np.errstate(invalid="ignore"):
+        want = A.astype(np.float64) @ B.astype(np.float64)
+    dA, dB, dC = dev(cuda, A), dev(cuda, B), dev(cuda, np.zeros((m, n), np.float32))
+    capi.gemm_f32(0, 0, dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), m, n, k, 0.0)
+    got = host(dC).astype(np.float64)
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(want))
+    np.testing.assert_array_equal(np.isposinf(got), np.isposinf(want))
+    np.testing.assert_array_equal(np.isneginf(got), np.isneginf(want))
+    fin = np.isfinite(want)
+    assert rel_err(got[fin], want[fin]) <= 1e-5
+
+
 def test_memory_ops(cuda):
     rng = np.random.default_rng(1)
     for dt in NP_DTYPES:
