@@ -72,6 +72,16 @@ constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KB
 // the big accumulator.
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// CTA-pair kernel (cta_group::2): 256 x BN tiles, each CTA loading 128 rows
+// of A and 128 rows (half) of B per k-block.
+constexpr int P_STAGES = 6;
+constexpr int P_A_TILE = 128 * BK * 2;                       // 8 KB
+constexpr int P_B_TILE = 128 * BK * 2;                       // 8 KB: half of N
+constexpr int P_STAGE_BYTES = 2 * P_A_TILE + 2 * P_B_TILE;  // 32 KB per CTA
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_TM = 256;  // output tile rows per pair
+constexpr int kThreadsP = 320;  // producer, MMA, 8 epilogue warps
+
 constexpr long long kWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
 
 // Device error word: 0 = ok, else the code of the first bounded wait that expired.
@@ -163,6 +173,30 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])::"memory");  // uses of r stay after the wait
+}
+
+// tcgen05.ld without the wait, so several loads can be in flight.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Orders every use of r after the preceding tcgen05.wait::ld: the registers
+// of an asynchronous tcgen05.ld are only valid once the wait has returned.
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])::"memory");
 }
 
 // ------------------------------------------------------------ split pass
@@ -209,11 +243,11 @@ __device__ __forceinline__ float block_max256(float v, float* red) {
 
 // src is [rows, K] row-major (K-major already).  One CTA per row at a time:
 // the row's finite max-abs, then hi/lo [rows, Kp] with zero padding; rowmax
-// receives the max for the epilogue.  vec: K % 4 == 0 and src 16-byte aligned.
+// receives the max and expo the row's scale exponent (for the epilogue).  vec: K % 4 == 0 and src 16-byte aligned.
 template <bool vec>
 __global__ void __launch_bounds__(256)
     split_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp, __half* __restrict__ hi,
-                      __half* __restrict__ lo, float* __restrict__ rowmax) {
+                      __half* __restrict__ lo, float* __restrict__ rowmax, int* __restrict__ expo) {
   __shared__ float red[8];
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float* row = src + r * K;
@@ -228,8 +262,11 @@ __global__ void __launch_bounds__(256)
       for (int64_t c = threadIdx.x; c < K; c += 256) mx = fmaxf(mx, finite_abs(__ldg(row + c)));
     }
     mx = block_max256(mx, red);
-    if (threadIdx.x == 0) rowmax[r] = mx;
     const int e = row_exp(mx);
+    if (threadIdx.x == 0) {
+      rowmax[r] = mx;
+      expo[r] = e;
+    }
     __half* hrow = hi + r * Kp;
     __half* lrow = lo + r * Kp;
     if (vec) {  // Kp % 4 == 0; 4 halves = 8 bytes per store
@@ -281,7 +318,8 @@ __global__ void __launch_bounds__(256)
 // K both coalesced.
 __global__ void __launch_bounds__(256)
     split_transpose_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
-                           const float* __restrict__ colmax, __half* __restrict__ hi, __half* __restrict__ lo) {
+                           const float* __restrict__ colmax, __half* __restrict__ hi, __half* __restrict__ lo,
+                           int* __restrict__ expo) {
   __shared__ float tile[64][65];
   const int64_t k0 = (int64_t)blockIdx.y * 64, r0 = (int64_t)blockIdx.x * 64;
   {
@@ -300,6 +338,7 @@ __global__ void __launch_bounds__(256)
     const int64_t r = r0 + j;
     if (r < rows && k < Kp) {  // Kp is even, so k + 1 < Kp too
       const int e = row_exp(__ldg(colmax + r));
+      if (blockIdx.y == 0 && kx == 0) expo[r] = e;  // once per row
       __half h0, h1, l0, l1;
       split16(pow2_scale(tile[2 * kx][j], e), h0, l0);
       split16(pow2_scale(tile[2 * kx + 1][j], e), h1, l1);
@@ -323,11 +362,75 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   n0 = (local / gsize) * BN;
 }
 
+// As tile_coords, for the pair kernel's 256-row tiles.
+__device__ __forceinline__ void tile_coords_pair(int t, int tiles_m, int tiles_n, int& m0, int& n0) {
+  const int group = 8;
+  const int g = t / (group * tiles_n);
+  const int first_m = g * group;
+  const int gsize = min(tiles_m - first_m, group);
+  const int local = t % (group * tiles_n);
+  m0 = (first_m + local % gsize) * P_TM;
+  n0 = (local / gsize) * BN;
+}
+
+// Epilogue of one tile for one thread: TMEM lane `taddr` (this warp's lane
+// quarter) holds output row `row`, columns [n0, n0 + BN): big accumulator at
+// column offset 0, cross terms at BN.  Combines, unscales, adds C when beta,
+// stores.  Every thread of the warp must call it (tcgen05.ld is warp-wide).
+__device__ __forceinline__ void drain_tile(uint32_t taddr, int row, int n0, int M, int N,
+                                           const int* __restrict__ eA, const int* __restrict__ eB,
+                                           float* __restrict__ C, int beta, bool ok) {
+  const bool vec = (N & 3) == 0;
+  const int erow = row < M ? __ldg(eA + row) : 0;
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 16) {
+    uint32_t r[16], rs[16];
+    tmem_ld16(taddr + c, r);
+    tmem_ld16(taddr + BN + c, rs);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      // an infinite hi*hi sum stands: its cross terms may hold inf*0 = NaN
+      const float big = __uint_as_float(r[j]);
+      r[j] = __float_as_uint(isinf(big) ? big : __fmaf_rn(__uint_as_float(rs[j]), 0x1p-11f, big));
+    }
+    if (!ok || row >= M) continue;
+    float* crow = C + (int64_t)row * N + n0 + c;
+    const int ncols = min(16, N - (n0 + c));
+    if (ncols <= 0) continue;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int col = min(n0 + c + j, N - 1);
+      r[j] = __float_as_uint(pow2_scale(__uint_as_float(r[j]), -(erow + __ldg(eB + col))));
+    }
+    if (vec && ncols == 16) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 4) {
+        float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                               __uint_as_float(r[j + 3]));
+        if (beta) {
+          const float4 o = *reinterpret_cast<const float4*>(crow + j);
+          v.x = __fadd_rn(o.x, v.x);
+          v.y = __fadd_rn(o.y, v.y);
+          v.z = __fadd_rn(o.z, v.z);
+          v.w = __fadd_rn(o.w, v.w);
+        }
+        *reinterpret_cast<float4*>(crow + j) = v;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) {
+        float v = __uint_as_float(r[j]);
+        if (beta) v = __fadd_rn(crow[j], v);
+        crow[j] = v;
+      }
+    }
+  }
+}
+
 // Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                       const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
-                      const float* __restrict__ maxA, const float* __restrict__ maxB, float* __restrict__ C, int M,
+                      const int* __restrict__ eA, const int* __restrict__ eB, float* __restrict__ C, int M,
                       int N, int num_kb, int beta, int tiles_m, int tiles_n) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -424,7 +527,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2) {
     // ---- epilogue: TMEM -> registers -> global, one tile behind the MMAs
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const bool vec = (N & 3) == 0;
     int lt = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
       const uint32_t aphase = lt & 1;
@@ -433,50 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m0, n0;
       tile_coords(t, tiles_m, tiles_n, m0, n0);
       const int row = m0 + q * 32 + lane;
-      const int erow = row < M ? row_exp(__ldg(maxA + row)) : 0;
-      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16], rs[16];
-        tmem_ld16(taddr + c, r);
-        tmem_ld16(taddr + BN + c, rs);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // an infinite hi*hi sum stands: its cross terms may hold inf*0 = NaN
-          const float big = __uint_as_float(r[j]);
-          r[j] = __float_as_uint(isinf(big) ? big : __fmaf_rn(__uint_as_float(rs[j]), 0x1p-11f, big));
-        }
-        if (!ok || row >= M) continue;
-        float* crow = C + (int64_t)row * N + n0 + c;
-        const int ncols = min(16, N - (n0 + c));
-        if (ncols <= 0) continue;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int col = min(n0 + c + j, N - 1);
-          r[j] = __float_as_uint(pow2_scale(__uint_as_float(r[j]), -(erow + row_exp(__ldg(maxB + col)))));
-        }
-        if (vec && ncols == 16) {
-#pragma unroll
-          for (int j = 0; j < 16; j += 4) {
-            float4 v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                   __uint_as_float(r[j + 3]));
-            if (beta) {
-              const float4 o = *reinterpret_cast<const float4*>(crow + j);
-              v.x = __fadd_rn(o.x, v.x);
-              v.y = __fadd_rn(o.y, v.y);
-              v.z = __fadd_rn(o.z, v.z);
-              v.w = __fadd_rn(o.w, v.w);
-            }
-            *reinterpret_cast<float4*>(crow + j) = v;
-          }
-        } else {
-          for (int j = 0; j < ncols; ++j) {
-            float v = __uint_as_float(r[j]);
-            if (beta) v = __fadd_rn(crow[j], v);
-            crow[j] = v;
-          }
-        }
-      }
+      drain_tile(tmem + ((uint32_t)(q * 32) << 16), row, n0, M, N, eA, eB, C, beta, ok);
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[0]));
       if (!ok) break;
@@ -487,6 +546,254 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ CTA-pair kernel
+//
+// Two CTAs of a cluster compute one 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA loads its own 128 rows of A
+// and its half (128 rows) of B, so a k-block costs each SM 32 KB of loads
+// instead of 48 KB, and six stages fit where four did.  The even CTA (the
+// leader) issues the MMAs; its `full` barriers collect the load bytes of
+// both CTAs (the .cta_group::2 form of the TMA load signals the leader's
+// barrier; no load is multicast), and its commits arrive on the `empty` and
+// `tfull` barriers of both CTAs.  Each CTA's TMEM holds its 128 rows; both
+// epilogues drain their own half and arrive on the leader's `tempty`.
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `cta` of the cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t addr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// TMA tile load into this CTA's shared memory; completion bytes go to the
+// mbarrier at `bar` (a cluster address, here the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive on the barrier at this shared offset in both CTAs of the pair once
+// the leader's issued MMAs complete.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+// kind::f16, D f32, A and B f16, K-major, M = 256 (across the pair), N = BN.
+__host__ __device__ constexpr uint32_t instr_desc_pair() {
+  return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(P_TM >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(kThreadsP, 1)
+    gemm_f16x3_pair_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
+                           const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
+                           const int* __restrict__ eA, const int* __restrict__ eB, float* __restrict__ C, int M,
+                           int N, int num_kb, int beta, int tiles_m, int tiles_n) {
+  extern __shared__ uint8_t smem_raw[];
+  // The same offsets in both CTAs: the pair MMA addresses the peer's tiles
+  // and the commits address the peer's barriers by the local offset.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_tiles = tiles_m * tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);   // the leader's expect_tx
+      mbar_init(smem_u32(&empty[s]), 1);  // the leader's commit
+    }
+    mbar_init(smem_u32(&tfull[0]), 1);
+    mbar_init(smem_u32(&tempty[0]), 16);  // one arrive per epilogue warp, both CTAs
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer, both CTAs
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAh)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tAl)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBh)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBl)) : "memory");
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += npairs) {
+      int m0, n0;
+      tile_coords_pair(t, tiles_m, tiles_n, m0, n0);
+      const int ya = m0 + (int)rank * 128, yb = n0 + (int)rank * 128;
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % P_STAGES;
+        const uint32_t phase = (it / P_STAGES) & 1;
+        if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, 5)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * P_STAGE_BYTES;
+        const uint32_t bar_local = smem_u32(&full[s]);
+        if (leader) mbar_expect_tx(bar_local, 2 * P_STAGE_BYTES);
+        const uint32_t bar = map_to_cta(bar_local, 0);
+        tma_load_2d_pair(smem_u32(st), &tAh, kb * BK, ya, bar);
+        tma_load_2d_pair(smem_u32(st + P_A_TILE), &tAl, kb * BK, ya, bar);
+        tma_load_2d_pair(smem_u32(st + 2 * P_A_TILE), &tBh, kb * BK, yb, bar);
+        tma_load_2d_pair(smem_u32(st + 2 * P_A_TILE + P_B_TILE), &tBl, kb * BK, yb, bar);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---- MMA issuer, leader only
+    constexpr uint32_t idesc = instr_desc_pair();
+    uint32_t it = 0;
+    bool ok = true;
+    int lt = 0;
+    for (int t = pair; t < num_tiles && ok; t += npairs, ++lt) {
+      if (!mbar_wait(smem_u32(&tempty[0]), (lt & 1) ^ 1, 6)) break;  // both epilogues drained
+      tc_fence_after();
+      const uint32_t dbig = tmem, dsmall = tmem + (uint32_t)BN;
+      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        const int s = it % P_STAGES;
+        const uint32_t phase = (it / P_STAGES) & 1;
+        if (!mbar_wait(smem_u32(&full[s]), phase, 7)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = smem_u32(smem + s * P_STAGE_BYTES);
+        const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + P_A_TILE);
+        const uint64_t dBh = smem_desc(base + 2 * P_A_TILE), dBl = smem_desc(base + 2 * P_A_TILE + P_B_TILE);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t off = (uint64_t)((kk * 32) >> 4);
+          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+          mma_f16_pair(dsmall, dAl + off, dBh + off, idesc, first);
+          mma_f16_pair(dsmall, dAh + off, dBl + off, idesc, 1u);
+          mma_f16_pair(dbig, dAh + off, dBh + off, idesc, first);
+        }
+        mma_commit_pair(smem_u32(&empty[s]));
+      }
+      mma_commit_pair(smem_u32(&tfull[0]));
+    }
+  } else if (warp >= 2) {
+    // ---- epilogue, both CTAs: this CTA's 128 rows of the pair's tile.  Two
+    // warps per TMEM lane quarter, one per 128-column half.  Each thread
+    // pulls its 128 combined values into registers and releases the
+    // accumulators before unscaling and storing, so the stores overlap the
+    // next tile's MMAs.
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
+    const uint32_t tempty_leader = map_to_cta(smem_u32(&tempty[0]), 0);
+    const bool vec = (N & 3) == 0;
+    int lt = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++lt) {
+      const bool ok = mbar_wait(smem_u32(&tfull[0]), lt & 1, 8);
+      tc_fence_after();
+      int m0, n0;
+      tile_coords_pair(t, tiles_m, tiles_n, m0, n0);
+      const int row = m0 + (int)rank * 128 + q * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+      float v[128];
+#pragma unroll
+      for (int c = 0; c < 128; c += 16) {
+        uint32_t rb[16], rs[16];
+        tmem_ld16_issue(taddr + c, rb);
+        tmem_ld16_issue(taddr + BN + c, rs);
+        tmem_ld_wait();
+        tmem_regs_ready(rb);
+        tmem_regs_ready(rs);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // an infinite hi*hi sum stands: its cross terms may hold inf*0 = NaN
+          const float big = __uint_as_float(rb[j]);
+          v[c + j] = isinf(big) ? big : __fmaf_rn(__uint_as_float(rs[j]), 0x1p-11f, big);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader);
+      if (ok && row < M) {
+        const int erow = __ldg(eA + row);
+        const int c0 = n0 + h * 128;
+        float* crow = C + (int64_t)row * N + c0;
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          const int col = c0 + c;
+          if (vec && col + 3 < N) {
+            const int4 ec = __ldg(reinterpret_cast<const int4*>(eB + col));
+            float4 o = make_float4(pow2_scale(v[c], -(erow + ec.x)), pow2_scale(v[c + 1], -(erow + ec.y)),
+                                   pow2_scale(v[c + 2], -(erow + ec.z)), pow2_scale(v[c + 3], -(erow + ec.w)));
+            if (beta) {
+              const float4 p = *reinterpret_cast<const float4*>(crow + c);
+              o.x = __fadd_rn(p.x, o.x);
+              o.y = __fadd_rn(p.y, o.y);
+              o.z = __fadd_rn(p.z, o.z);
+              o.w = __fadd_rn(p.w, o.w);
+            }
+            *reinterpret_cast<float4*>(crow + c) = o;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (col + i < N) {
+                float o = pow2_scale(v[c + i], -(erow + __ldg(eB + col + i)));
+                if (beta) o = __fadd_rn(crow[c + i], o);
+                crow[c + i] = o;
+              }
+          }
+        }
+      }
+      if (!ok) break;
+    }
+  }
+  // Neither CTA may leave while the other can still reach its shared memory
+  // or TMEM.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -523,17 +830,44 @@ lmpb_status make_map(CUtensorMap* map, const __half* base, int64_t rows, int64_t
   return LMPB_OK;
 }
 
+// How many CTA pairs of the pair kernel can be resident at once on the
+// current device (the persistent grid's size in pairs); 0 if none.
+int pair_clusters() {
+  static int cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cached[dev] > 0) return cached[dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)sm_count());
+  cfg.blockDim = dim3(kThreadsP);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_f16x3_pair_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cached[dev] = n;
+  return n;
+}
+
 // One operand -> scaled fp16 hi/lo planes [rows, Kp] and its row maxima.
 // kmajor: src is [rows, K]; else src is [K, rows].  rowmax must be zeroed
 // beforehand when !kmajor.
 lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K, int64_t Kp, __half* hi,
-                          __half* lo, float* rowmax, cudaStream_t st) {
+                          __half* lo, float* rowmax, int* expo, cudaStream_t st) {
   if (kmajor) {
     const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)sm_count() * 8));
     if ((K & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0)
-      split_rows_kernel<true><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax);
+      split_rows_kernel<true><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
     else
-      split_rows_kernel<false><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax);
+      split_rows_kernel<false><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
     return launch_status("gemm split pass (rows)");
   }
   if ((Kp + 63) / 64 > 65535 || (K + 255) / 256 > 65535)
@@ -543,7 +877,7 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
   lmpb_status s = launch_status("gemm split pass (column maxima)");
   if (s != LMPB_OK) return s;
   split_transpose_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64)), 256, 0, st>>>(
-      src, rows, K, Kp, rowmax, hi, lo);
+      src, rows, K, Kp, rowmax, hi, lo, expo);
   return launch_status("gemm split pass (transpose)");
 }
 
@@ -559,20 +893,25 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_f16x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      P_SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(attr_err));
   const int64_t Kp = (k + BK - 1) / BK * BK;
   auto up = [](size_t b) { return (b + 255) / 256 * 256; };
   const size_t plane_a = up((size_t)m * Kp * 2), plane_b = up((size_t)n * Kp * 2);
-  const size_t max_a = up((size_t)m * 4), max_b = up((size_t)n * 4);
+  const size_t max_a = up((size_t)m * 4), max_b = up((size_t)n * 4);  // row maxima, then row exponents
   char* ws = nullptr;
-  LMPB_CUDA_TRY(stream_alloc((void**)&ws, 2 * plane_a + 2 * plane_b + max_a + max_b, st));
+  LMPB_CUDA_TRY(stream_alloc((void**)&ws, 2 * plane_a + 2 * plane_b + 2 * (max_a + max_b), st));
   __half* Ah = reinterpret_cast<__half*>(ws);
   __half* Al = reinterpret_cast<__half*>(ws + plane_a);
   __half* Bh = reinterpret_cast<__half*>(ws + 2 * plane_a);
   __half* Bl = reinterpret_cast<__half*>(ws + 2 * plane_a + plane_b);
   float* mxA = reinterpret_cast<float*>(ws + 2 * plane_a + 2 * plane_b);
   float* mxB = reinterpret_cast<float*>(ws + 2 * plane_a + 2 * plane_b + max_a);
+  int* exA = reinterpret_cast<int*>(ws + 2 * plane_a + 2 * plane_b + max_a + max_b);
+  int* exB = reinterpret_cast<int*>(ws + 2 * plane_a + 2 * plane_b + 2 * max_a + max_b);
   // op(A) is [m,k]: K-major as stored unless transposed; the MMA's B operand
   // is op(B)^T = [n,k]: K-major as stored only when trans_b.
   const bool ka = !trans_a, kb = trans_b != 0;
@@ -581,25 +920,53 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
     const cudaError_t e = cudaMemsetAsync(ws + 2 * plane_a + 2 * plane_b, 0, max_a + max_b, st);
     if (e != cudaSuccess) s = set_error(LMPB_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
   }
-  if (s == LMPB_OK) s = split_operand(A, ka, m, k, Kp, Ah, Al, mxA, st);
-  if (s == LMPB_OK) s = split_operand(B, kb, n, k, Kp, Bh, Bl, mxB, st);
+  if (s == LMPB_OK) s = split_operand(A, ka, m, k, Kp, Ah, Al, mxA, exA, st);
+  if (s == LMPB_OK) s = split_operand(B, kb, n, k, Kp, Bh, Bl, mxB, exB, st);
+  // Pair kernel when there are 256 rows to pair up; the single-CTA kernel
+  // otherwise (LMPB_GEMM_PAIR=0 forces it, for comparison).
+  static const bool pair_off = [] {
+    const char* v = getenv("LMPB_GEMM_PAIR");
+    return v && v[0] == '0';
+  }();
+  const bool pair = m >= P_TM && !pair_off;
   CUtensorMap mAh, mAl, mBh, mBl;
+  const int b_box = pair ? BN / 2 : BN;
   if (s == LMPB_OK) s = make_map(&mAh, Ah, m, Kp, BM);
   if (s == LMPB_OK) s = make_map(&mAl, Al, m, Kp, BM);
-  if (s == LMPB_OK) s = make_map(&mBh, Bh, n, Kp, BN);
-  if (s == LMPB_OK) s = make_map(&mBl, Bl, n, Kp, BN);
-  if (s == LMPB_OK) {
-    const int64_t tiles_n = (n + BN - 1) / BN, tiles_m = (m + BM - 1) / BM;
-    if (tiles_m * tiles_n > 0x7FFFFFFF) {
-      s = set_error(LMPB_ERR_UNSUPPORTED, "gemm: too many tiles");
+  if (s == LMPB_OK) s = make_map(&mBh, Bh, n, Kp, b_box);
+  if (s == LMPB_OK) s = make_map(&mBl, Bl, n, Kp, b_box);
+  const int64_t tiles_n = (n + BN - 1) / BN, tiles_m = (m + (pair ? P_TM : BM) - 1) / (pair ? P_TM : BM);
+  if (s == LMPB_OK && tiles_m * tiles_n > 0x7FFFFFFF) s = set_error(LMPB_ERR_UNSUPPORTED, "gemm: too many tiles");
+  const int64_t ntiles = tiles_m * tiles_n;
+  const int nkb = (int)(Kp / BK), bflag = beta != 0.f ? 1 : 0;
+  if (s == LMPB_OK && pair) {
+    int clusters = pair_clusters();
+    if (clusters <= 0) {
+      s = set_error(LMPB_ERR_CUDA, "gemm: no CTA-pair cluster fits on this device");
     } else {
-      const int64_t ntiles = tiles_m * tiles_n;
-      const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
-      gemm_f16x3_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, mxA, mxB, C, (int)m, (int)n,
-                                                            (int)(Kp / BK), beta != 0.f ? 1 : 0, (int)tiles_m,
-                                                            (int)tiles_n);
-      s = launch_status("gemm_f16x3_kernel");
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, clusters)));
+      cfg.blockDim = dim3(kThreadsP);
+      cfg.dynamicSmemBytes = P_SMEM_BYTES;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_f16x3_pair_kernel, mAh, mAl, mBh, mBl, (const int*)exA,
+                                                (const int*)exB, C, (int)m, (int)n, nkb, bflag, (int)tiles_m,
+                                                (int)tiles_n);
+      s = le != cudaSuccess ? set_error(LMPB_ERR_CUDA, std::string("gemm pair launch: ") + cudaGetErrorString(le))
+                            : launch_status("gemm_f16x3_pair_kernel");
     }
+  } else if (s == LMPB_OK) {
+    const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
+    gemm_f16x3_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, exA, exB, C, (int)m, (int)n, nkb, bflag,
+                                                          (int)tiles_m, (int)tiles_n);
+    s = launch_status("gemm_f16x3_kernel");
   }
   cudaError_t e = cudaFreeAsync(ws, st);
   if (s == LMPB_OK && e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("cudaFreeAsync: ") + cudaGetErrorString(e));
