@@ -188,6 +188,19 @@ lmpb_status lmpb_matmul(int out_dtype, const void* A, int a_dtype, const void* B
 lmpb_status lmpb_gemm_f32(int trans_a, int trans_b, const float* A, const float* B, float* C,
                           int64_t m, int64_t n, int64_t k, float beta, void* stream);
 
+/* C[m,n] = clamp(op(A)·op(B) + bias, lo, hi) in one tensor-core GEMM: the
+ * bias row (n fp32 values, broadcast over the rows; null for none) and the
+ * clamp (when `clamp` is non-zero) run in the GEMM's epilogue, rounding and
+ * comparing exactly as the eager ADD and CLAMP kernels do, so the result is
+ * bit-identical to lmpb_gemm_f32 followed by lmpb_binary(ADD, C, bias) and
+ * lmpb_unary(CLAMP).  This is the Linear(+ReLU) of the reference's layers
+ * (matmul, broadcast add, clamp(0, DBL_MAX): python layers/linear.py,
+ * layers/activation.py) without writing and re-reading the product.  No
+ * single counterpart in the reference, which runs the three ops apart. */
+lmpb_status lmpb_gemm_f32_bias_act(int trans_a, int trans_b, const float* A, const float* B, float* C,
+                                   int64_t m, int64_t n, int64_t k, const float* bias, int clamp,
+                                   double lo, double hi, void* stream);
+
 /* LMPB_ERR_TIMEOUT if a bounded device wait inside a kernel expired since
  * the last call (the kernel then stopped early and its output is invalid),
  * else LMPB_OK.  Synchronises the current device.  No counterpart in the

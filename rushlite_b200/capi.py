@@ -42,6 +42,7 @@ EXPORTS = [
     "lmpb_reduce", "lmpb_matmul", "lmpb_gemm_f32", "lmpb_transpose", "lmpb_malloc", "lmpb_free",
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
     "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error", "lmpb_reduce_noalloc",
+    "lmpb_gemm_f32_bias_act",
 ]
 
 
@@ -85,6 +86,7 @@ def lib() -> C.CDLL:
         L.lmpb_reduce_noalloc.argtypes = [i32, i32, vp, P64, i32, i32, vp, vp]
         L.lmpb_matmul.argtypes = [i32, vp, i32, vp, i32, vp, i64, i64, i64, vp]
         L.lmpb_gemm_f32.argtypes = [i32, i32, vp, vp, vp, i64, i64, i64, C.c_float, vp]
+        L.lmpb_gemm_f32_bias_act.argtypes = [i32, i32, vp, vp, vp, i64, i64, i64, vp, i32, d, d, vp]
         L.lmpb_transpose.argtypes = [i32, vp, vp, i64, i64, vp]
         L.lmpb_device_error.argtypes = []
         L.lmpb_malloc.argtypes = [C.POINTER(vp), C.c_size_t, vp]
@@ -141,6 +143,10 @@ def matmul(out_dt, a_ptr, a_dt, b_ptr, b_dt, c_ptr, m, k, n, stream=0):
 
 def gemm_f32(ta, tb, a_ptr, b_ptr, c_ptr, m, n, k, beta=0.0, stream=0):
     check(lib().lmpb_gemm_f32(ta, tb, a_ptr, b_ptr, c_ptr, m, n, k, beta, stream))
+
+
+def gemm_f32_bias_act(ta, tb, a_ptr, b_ptr, c_ptr, m, n, k, bias_ptr=None, clamp=0, lo=0.0, hi=0.0, stream=0):
+    check(lib().lmpb_gemm_f32_bias_act(ta, tb, a_ptr, b_ptr, c_ptr, m, n, k, bias_ptr, clamp, lo, hi, stream))
 
 
 def transpose(dt, in_ptr, out_ptr, m, n, stream=0):

@@ -373,13 +373,29 @@ __device__ __forceinline__ void tile_coords_pair(int t, int tiles_m, int tiles_n
   n0 = (local / gsize) * BN;
 }
 
+// Optional epilogue after the product: + bias[col] (a row of n, fp32) then
+// clamp(lo, hi), each rounding and comparing as the eager elementwise kernels
+// do (fp32 add; a < lo ? lo : (a > hi ? hi : a)), so a fused Linear+ReLU is
+// bit-identical to matmul, + bias, clamp run one after another.
+struct Epilogue {
+  const float* bias;  // null: none
+  int clamp;
+  float lo, hi;
+};
+
+__device__ __forceinline__ float epilogue_apply(const Epilogue& ep, float v, int col) {
+  if (ep.bias) v = __fadd_rn(v, __ldg(ep.bias + col));
+  if (ep.clamp) v = v < ep.lo ? ep.lo : (v > ep.hi ? ep.hi : v);
+  return v;
+}
+
 // Epilogue of one tile for one thread: TMEM lane `taddr` (this warp's lane
 // quarter) holds output row `row`, columns [n0, n0 + BN): big accumulator at
 // column offset 0, cross terms at BN.  Combines, unscales, adds C when beta,
 // stores.  Every thread of the warp must call it (tcgen05.ld is warp-wide).
 __device__ __forceinline__ void drain_tile(uint32_t taddr, int row, int n0, int M, int N,
                                            const int* __restrict__ eA, const int* __restrict__ eB,
-                                           float* __restrict__ C, int beta, bool ok) {
+                                           float* __restrict__ C, int beta, bool ok, const Epilogue& ep) {
   const bool vec = (N & 3) == 0;
   const int erow = row < M ? __ldg(eA + row) : 0;
 #pragma unroll 1
@@ -401,6 +417,11 @@ __device__ __forceinline__ void drain_tile(uint32_t taddr, int row, int n0, int 
     for (int j = 0; j < 16; ++j) {
       const int col = min(n0 + c + j, N - 1);
       r[j] = __float_as_uint(pow2_scale(__uint_as_float(r[j]), -(erow + __ldg(eB + col))));
+    }
+    if (ep.bias || ep.clamp) {  // beta is 0 whenever an epilogue is given
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        r[j] = __float_as_uint(epilogue_apply(ep, __uint_as_float(r[j]), min(n0 + c + j, N - 1)));
     }
     if (vec && ncols == 16) {
 #pragma unroll
@@ -431,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                       const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                       const int* __restrict__ eA, const int* __restrict__ eB, float* __restrict__ C, int M,
-                      int N, int num_kb, int beta, int tiles_m, int tiles_n) {
+                      int N, int num_kb, int beta, int tiles_m, int tiles_n, Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -535,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m0, n0;
       tile_coords(t, tiles_m, tiles_n, m0, n0);
       const int row = m0 + q * 32 + lane;
-      drain_tile(tmem + ((uint32_t)(q * 32) << 16), row, n0, M, N, eA, eB, C, beta, ok);
+      drain_tile(tmem + ((uint32_t)(q * 32) << 16), row, n0, M, N, eA, eB, C, beta, ok, ep);
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[0]));
       if (!ok) break;
@@ -617,7 +638,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     gemm_f16x3_pair_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                            const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                            const int* __restrict__ eA, const int* __restrict__ eB, float* __restrict__ C, int M,
-                           int N, int num_kb, int beta, int tiles_m, int tiles_n) {
+                           int N, int num_kb, int beta, int tiles_m, int tiles_n, Epilogue ep) {
   extern __shared__ uint8_t smem_raw[];
   // The same offsets in both CTAs: the pair MMA addresses the peer's tiles
   // and the commits address the peer's barriers by the local offset.
@@ -764,6 +785,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             const int4 ec = __ldg(reinterpret_cast<const int4*>(eB + col));
             float4 o = make_float4(pow2_scale(v[c], -(erow + ec.x)), pow2_scale(v[c + 1], -(erow + ec.y)),
                                    pow2_scale(v[c + 2], -(erow + ec.z)), pow2_scale(v[c + 3], -(erow + ec.w)));
+            if (ep.bias || ep.clamp) {
+              o.x = epilogue_apply(ep, o.x, col);
+              o.y = epilogue_apply(ep, o.y, col + 1);
+              o.z = epilogue_apply(ep, o.z, col + 2);
+              o.w = epilogue_apply(ep, o.w, col + 3);
+            }
             if (beta) {
               const float4 p = *reinterpret_cast<const float4*>(crow + c);
               o.x = __fadd_rn(p.x, o.x);
@@ -778,6 +805,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
               if (col + i < N) {
                 float o = pow2_scale(v[c + i], -(erow + __ldg(eB + col + i)));
                 if (beta) o = __fadd_rn(crow[c + i], o);
+                o = epilogue_apply(ep, o, col + i);
                 crow[c + i] = o;
               }
           }
@@ -885,10 +913,21 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
 
 // Tensor-core path for problems that fill 128-row tiles; SIMT otherwise.
 lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float* B, float* C, int64_t m,
-                           int64_t n, int64_t k, float beta, cudaStream_t st) {
+                           int64_t n, int64_t k, float beta, cudaStream_t st, const float* bias, int clamp,
+                           double lo, double hi) {
+  const Epilogue ep{bias, clamp, (float)lo, (float)hi};
   const bool small = m < 64 || n < 64 || k < 32 || (double)m * n * k < 2.0e6;
   if (small || m > (1ll << 30) || n > (1ll << 30) || getenv("LMPB_GEMM_SIMT"))
-    return gemm_f32_simt(trans_a, trans_b, A, B, C, m, n, k, beta, st);
+  {
+    lmpb_status s = gemm_f32_simt(trans_a, trans_b, A, B, C, m, n, k, beta, st);
+    // the eager elementwise kernels, in place: the same values as the fused epilogue
+    if (s == LMPB_OK && bias) {
+      const int64_t cs[2] = {m, n}, bs[1] = {n};
+      s = lmpb_binary(LMPB_ADD, LMPB_FLOAT32, C, LMPB_FLOAT32, cs, 2, bias, LMPB_FLOAT32, bs, 1, C, 0.0, 0.0, st);
+    }
+    if (s == LMPB_OK && clamp) s = lmpb_unary(LMPB_CLAMP, LMPB_FLOAT32, C, C, m * n, lo, hi, st);
+    return s;
+  }
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
@@ -958,14 +997,14 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
       cfg.numAttrs = 1;
       const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_f16x3_pair_kernel, mAh, mAl, mBh, mBl, (const int*)exA,
                                                 (const int*)exB, C, (int)m, (int)n, nkb, bflag, (int)tiles_m,
-                                                (int)tiles_n);
+                                                (int)tiles_n, ep);
       s = le != cudaSuccess ? set_error(LMPB_ERR_CUDA, std::string("gemm pair launch: ") + cudaGetErrorString(le))
                             : launch_status("gemm_f16x3_pair_kernel");
     }
   } else if (s == LMPB_OK) {
     const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
     gemm_f16x3_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, exA, exB, C, (int)m, (int)n, nkb, bflag,
-                                                          (int)tiles_m, (int)tiles_n);
+                                                          (int)tiles_m, (int)tiles_n, ep);
     s = launch_status("gemm_f16x3_kernel");
   }
   cudaError_t e = cudaFreeAsync(ws, st);

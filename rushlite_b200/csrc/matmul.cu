@@ -8,7 +8,8 @@ namespace lmpb {
 
 // Declared in gemm_sm100.cu.
 lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float* B, float* C,
-                           int64_t m, int64_t n, int64_t k, float beta, cudaStream_t st);
+                           int64_t m, int64_t n, int64_t k, float beta, cudaStream_t st,
+                           const float* bias = nullptr, int clamp = 0, double lo = 0.0, double hi = 0.0);
 unsigned int gemm_take_error();
 
 namespace {
@@ -72,6 +73,25 @@ extern "C" lmpb_status lmpb_gemm_f32(int trans_a, int trans_b, const float* A, c
   LMPB_CHECK_ARG(C != nullptr && (k == 0 || (A && B)), "lmpb_gemm_f32: null pointer");
   if (k == 0) return beta == 0.f ? lmpb_fill(LMPB_FLOAT32, C, m * n, 0.0, stream) : LMPB_OK;
   return gemm_f32_sm100(trans_a, trans_b, A, B, C, m, n, k, beta, as_stream(stream));
+}
+
+extern "C" lmpb_status lmpb_gemm_f32_bias_act(int trans_a, int trans_b, const float* A, const float* B,
+                                              float* C, int64_t m, int64_t n, int64_t k, const float* bias,
+                                              int clamp, double lo, double hi, void* stream) {
+  LMPB_CHECK_ARG(m >= 0 && n >= 0 && k >= 0, "lmpb_gemm_f32_bias_act: negative size");
+  if (m == 0 || n == 0) return LMPB_OK;
+  LMPB_CHECK_ARG(C != nullptr && (k == 0 || (A && B)), "lmpb_gemm_f32_bias_act: null pointer");
+  if (k == 0) {  // the product is zero: C = clamp(0 + bias)
+    cudaStream_t st = as_stream(stream);
+    lmpb_status s = lmpb_fill(LMPB_FLOAT32, C, m * n, 0.0, st);
+    if (s == LMPB_OK && bias) {
+      const int64_t cs[2] = {m, n}, bs[1] = {n};
+      s = lmpb_binary(LMPB_ADD, LMPB_FLOAT32, C, LMPB_FLOAT32, cs, 2, bias, LMPB_FLOAT32, bs, 1, C, 0.0, 0.0, st);
+    }
+    if (s == LMPB_OK && clamp) s = lmpb_unary(LMPB_CLAMP, LMPB_FLOAT32, C, C, m * n, lo, hi, st);
+    return s;
+  }
+  return gemm_f32_sm100(trans_a, trans_b, A, B, C, m, n, k, 0.f, as_stream(stream), bias, clamp, lo, hi);
 }
 
 extern "C" lmpb_status lmpb_device_error(void) {

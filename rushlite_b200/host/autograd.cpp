@@ -283,11 +283,17 @@ LMP_UN(sin, tops::sin(a.data()), tops::mul(g, tops::cos(self.data())))
 LMP_UN(cos, tops::cos(a.data()), tops::mul(tops::neg(tops::sin(self.data())), g))
 LMP_UN(tan, tops::tan(a.data()), tops::add(g, tops::mul(tops::mul(g, out.data()), out.data())))
 
+// ClampBackward (csrc/src/autograd/functions/unary_ops.cpp): g where
+// lo < x < hi.  It is evaluated on the output instead of the input: clamp
+// and its backward both compare in the tensor's dtype against the same cast
+// bounds, and the output is lo, hi or x, so lo < out < hi exactly when
+// lo < x < hi (NaN and lo > hi included).  The input then need not stay
+// materialised: a fused Linear+ReLU never writes its pre-activation.
 Variable clamp(const Variable& a, Scalar lo, Scalar hi) {
   Tensor r = tops::clamp(a.data(), lo, hi);
   return record(r, {a}, [lo, hi](const Variable& out, variable_list& in) {
     Variable& self = in[0];
-    if (self.requires_grad()) self.incr_grad(tops::clamp_backward(self.data(), out.grad(), lo, hi));
+    if (self.requires_grad()) self.incr_grad(tops::clamp_backward(out.data(), out.grad(), lo, hi));
   });
 }
 

@@ -87,9 +87,12 @@ using ImplPtr = std::shared_ptr<TensorImpl>;
 // Pending computation recorded under capture (csrc/include/lamp3/tensor/lazy/
 // lazy_function.hpp:11-22).  Elementwise nodes fuse through broadcasts;
 // ReduceSum (sum over the axes where the target shape is 1) fuses into the
-// kernel that produces its input, as an epilogue.
+// kernel that produces its input, as an epilogue.  Matmul (fp32) is pending
+// too, so that clamp(matmul + bias) and matmul + bias realize as one GEMM
+// with the bias and clamp in its epilogue; read any other way it realizes as
+// a plain GEMM.
 struct LazyNode {
-  enum Kind { kBinary, kUnary, kConst, kReduceSum };
+  enum Kind { kBinary, kUnary, kConst, kReduceSum, kMatmul };
   Kind kind;
   int op = 0;
   double p0 = 0.0, p1 = 0.0;  // clamp bounds / constant value

@@ -469,7 +469,7 @@ struct ProgramBuilder {
   static bool invariant_along(TensorImpl* t, const std::vector<size_t>& full, const std::vector<size_t>& target,
                               std::unordered_set<TensorImpl*>& seen) {
     if (!seen.insert(t).second) return true;
-    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum) {
+    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul) {
       const size_t nd = full.size();
       for (size_t k = 0; k < nd; ++k) {
         const size_t d = nd - 1 - k;
@@ -516,7 +516,8 @@ struct ProgramBuilder {
         return id;
       }
     }
-    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || nodes.size() > budget) {
+    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul ||
+        nodes.size() > budget) {
       id = leaf(t);  // realizes barriers / oversize sub-graphs first
     } else {
       LazyNode& L = *t->lazy;
@@ -722,6 +723,66 @@ void run_requests(std::vector<Request>& reqs) {
   }
 }
 
+// Writes the product of pending matmul node M (inputs A [m,k], B [k,n], fp32)
+// into `dst`'s storage; with `ep_of` (the target of a matched pattern) the
+// bias row and clamp of that pattern run in the GEMM's epilogue.
+struct EpilogueSpec {
+  TensorImpl* bias = nullptr;
+  bool clamp = false;
+  double lo = 0.0, hi = 0.0;
+};
+
+void run_matmul(TensorImpl* dst, TensorImpl* M, const EpilogueSpec* ep) {
+  if (!M) M = dst;
+  LazyNode& L = *M->lazy;
+  TensorImpl* A = L.inputs[0].get();
+  TensorImpl* B = L.inputs[1].get();
+  const int64_t m = (int64_t)A->shape[0], k = (int64_t)A->shape[1], n = (int64_t)B->shape[1];
+  const void* pa = A->data();
+  const void* pb = B->data();
+  const void* pbias = ep && ep->bias ? ep->bias->data() : nullptr;
+  if (!dst->storage || dst->storage->bytes < dst->nbytes()) dst->storage = make_storage(dst->nbytes(), dst->device);
+  float* pc = static_cast<float*>(dst->storage->ptr);
+  if (ep)
+    LMPB_OK_OR_THROW(lmpb_gemm_f32_bias_act(0, 0, static_cast<const float*>(pa), static_cast<const float*>(pb), pc,
+                                            m, n, k, static_cast<const float*>(pbias), ep->clamp ? 1 : 0, ep->lo,
+                                            ep->hi, g_stream));
+  else
+    LMPB_OK_OR_THROW(lmpb_matmul(LMPB_FLOAT32, pa, LMPB_FLOAT32, pb, LMPB_FLOAT32, pc, m, k, n, g_stream));
+  dst->lazy = nullptr;
+}
+
+// t = clamp(M + bias, lo, hi) or t = M + bias, with M a pending fp32 matmul
+// [m,n] and bias an fp32 row of n ([n] or [1,n]): one GEMM with the epilogue.
+// M itself stays pending (it realizes as a plain GEMM if it is ever read).
+bool gemm_epilogue(const ImplPtr& t) {
+  if (t->dtype != DataType::Float32 || t->shape.size() != 2 || t->storage) return false;
+  const size_t n = t->shape[1];
+  EpilogueSpec ep;
+  TensorImpl* add = t.get();
+  if (t->lazy->kind == LazyNode::kUnary && t->lazy->op == LMPB_CLAMP) {
+    ep.clamp = true;
+    ep.lo = t->lazy->p0;
+    ep.hi = t->lazy->p1;
+    add = t->lazy->inputs[0].get();
+  }
+  if (!add->lazy || add->storage || add->lazy->kind != LazyNode::kBinary || add->lazy->op != LMPB_ADD ||
+      add->dtype != DataType::Float32 || add->shape != t->shape)
+    return false;
+  for (int s = 0; s < 2; ++s) {
+    TensorImpl* M = add->lazy->inputs[s].get();
+    TensorImpl* b = add->lazy->inputs[1 - s].get();
+    const bool row = b->shape == std::vector<size_t>{n} || b->shape == std::vector<size_t>{1, n};
+    if (M->lazy && M->lazy->kind == LazyNode::kMatmul && !M->storage && M->shape == t->shape &&
+        b->dtype == DataType::Float32 && row) {
+      ep.bias = b;
+      run_matmul(t.get(), M, &ep);
+      return true;
+    }
+  }
+  return false;
+}
+
 }  // namespace
 
 // Realizes a batch of pending tensors.  A pending tensor whose expression is
@@ -741,6 +802,9 @@ void realize_all(const std::vector<ImplPtr>& ts) {
   for (const ImplPtr& t : pending) {
     const size_t n = t->numel();
     std::shared_ptr<LazyNode> L = t->lazy;
+    // (before storage is attached: a target that already has storage is a
+    // pending accumulation, which the fused GEMM must not overwrite)
+    if (n > 0 && gemm_epilogue(t)) continue;
     if (!t->storage || t->storage->bytes < t->nbytes()) t->storage = make_storage(t->nbytes(), t->device);
     if (n == 0) {
       t->lazy = nullptr;
@@ -749,6 +813,10 @@ void realize_all(const std::vector<ImplPtr>& ts) {
     if (L->kind == LazyNode::kConst) {
       LMPB_OK_OR_THROW(lmpb_fill((int)t->dtype, t->storage->ptr, (int64_t)n, L->p0, g_stream));
       t->lazy = nullptr;
+      continue;
+    }
+    if (L->kind == LazyNode::kMatmul) {
+      run_matmul(t.get(), nullptr, nullptr);
       continue;
     }
     if (L->kind == LazyNode::kReduceSum) {
@@ -924,6 +992,8 @@ Tensor matmul(const Tensor& a, const Tensor& b) {
   LMP_CHECK(a.shape()[1] == b.shape()[0], "matmul: inner dimensions " << a.shape()[1] << " and " << b.shape()[0] << " differ");
   const size_t m = a.shape()[0], k = a.shape()[1], n = b.shape()[1];
   const DataType dt = type_upcast(a.type(), b.type());
+  if (lazy::should_capture(a.device()) && a.type() == DataType::Float32 && b.type() == DataType::Float32)
+    return Tensor(record(LazyNode::kMatmul, 0, {a.impl(), b.impl()}, {m, n}, dt));
   ImplPtr out = new_impl({m, n}, dt, DeviceType::CUDA, true);
   const void* pa = a.impl()->data();
   const void* pb = b.impl()->data();
