@@ -59,6 +59,9 @@ struct StorageImpl {
   void* ptr = nullptr;
   size_t bytes = 0;
   DeviceType device = DeviceType::CPU;
+  // set when allocated while a Graph was capturing (graph memory): false
+  // once that capture was aborted, when the address was never backed
+  std::shared_ptr<const bool> graph_live;
   ~StorageImpl();
 };
 using Storage = std::shared_ptr<StorageImpl>;
@@ -183,6 +186,46 @@ void realize_all(const std::vector<ImplPtr>& ts);
 void set_stream(void* stream);
 void* current_stream();
 void synchronize();
+
+// CUDA-graph capture and replay of a repeated step (no counterpart in the
+// reference, which launches and synchronises every op).  Between
+// capture_begin() and capture_end() every kernel, copy, allocation and free
+// the host layer issues is recorded on a private stream instead of running;
+// replay() runs the recorded step again with one launch.  The recorded
+// addresses are fixed, so a replayable step updates its state in place
+// (Tensor::copy into the parameters, zero_grad) and reads no values on the
+// host.  Memory:
+//   * allocated during capture: graph memory at a fixed address, rewritten
+//     by each replay (a tensor created by the captured step shows the latest
+//     replay's values); freed inside the step, it is freed inside the graph;
+//   * allocated before and released during capture: kept until the Graph is
+//     destroyed, since every replay still reads it.
+// Build every fused program once before capturing (run the step once).
+class Graph {
+ public:
+  Graph() = default;
+  ~Graph();
+  Graph(const Graph&) = delete;
+  Graph& operator=(const Graph&) = delete;
+  void capture_begin();
+  void capture_end();
+  void capture_abort();  // ends a capture and discards it
+  void replay();
+  size_t kernels() const { return kernels_; }  // kernel nodes in the graph
+  void defer_free(void* p) { deferred_.push_back(p); }
+  const std::shared_ptr<bool>& live() const { return live_; }
+
+ private:
+  void* stream_ = nullptr;  // capture stream
+  void* prev_ = nullptr;    // the host layer's stream before capture; replays run on it
+  void* graph_ = nullptr;
+  void* exec_ = nullptr;
+  bool capturing_ = false;
+  size_t kernels_ = 0;
+  std::vector<void*> deferred_;
+  std::shared_ptr<bool> live_;
+};
+Graph* capturing_graph();
 
 namespace ops {
 Tensor add(const Tensor& a, const Tensor& b);

@@ -169,6 +169,25 @@ PYBIND11_MODULE(_C, m) {
   cuda.def("synchronize", []() { lmp::tensor::synchronize(); });
   cuda.def("kernel_launches", []() { return lmpb_kernel_launches(); },
            "Kernels launched by the backend library so far in this process.");
+  py::class_<lmp::tensor::Graph>(cuda, "Graph",
+                                 "CUDA-graph capture of a step: `with g:` records it (nothing runs), "
+                                 "g.replay() runs it again with one launch.  The step must update state in "
+                                 "place and read no values on the host; run it once before capturing.")
+      .def(py::init<>())
+      .def("capture_begin", &lmp::tensor::Graph::capture_begin)
+      .def("capture_end", &lmp::tensor::Graph::capture_end)
+      .def("replay", &lmp::tensor::Graph::replay, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("kernels", &lmp::tensor::Graph::kernels)
+      .def("__enter__", [](lmp::tensor::Graph& g) -> lmp::tensor::Graph& {
+             g.capture_begin();
+             return g;
+           }, py::return_value_policy::reference)
+      .def("capture_abort", &lmp::tensor::Graph::capture_abort)
+      .def("__exit__", [](lmp::tensor::Graph& g, py::object exc_type, py::object, py::object) {
+        if (exc_type.is_none()) g.capture_end();
+        else g.capture_abort();  // let the step's own exception propagate
+        return false;
+      });
 
   py::class_<lmp::tensor::HostCopy, std::shared_ptr<lmp::tensor::HostCopy>>(m, "_HostCopy")
       .def("wait", &lmp::tensor::HostCopy::wait, py::call_guard<py::gil_scoped_release>(),

@@ -44,6 +44,7 @@ void set_stream(void* s) { g_stream = s; }
 void* current_stream() { return g_stream; }
 void synchronize() {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(g_stream));
+  if (e != cudaSuccess) cudaGetLastError();  // reported here, not again by the next launch
   LMP_CHECK(e == cudaSuccess, "CUDA error: " << cudaGetErrorString(e));
 }
 
@@ -59,8 +60,28 @@ const char* dtype_name(DataType dt) {
 
 StorageImpl::~StorageImpl() {
   if (!ptr) return;
-  if (device == DeviceType::CUDA) lmpb_free(ptr, g_stream);
-  else std::free(ptr);
+  if (device != DeviceType::CUDA) {
+    std::free(ptr);
+    return;
+  }
+  if (graph_live && !*graph_live) return;  // its capture was aborted: nothing to free
+  Graph* g = capturing_graph();
+  if (g) {
+    // a capture already invalidated (an operation that cannot be recorded
+    // failed) accepts no further calls; its graph memory was never backed
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(g_stream), &cs) != cudaSuccess ||
+        cs == cudaStreamCaptureStatusInvalidated) {
+      cudaGetLastError();
+      if (!graph_live) g->defer_free(ptr);
+      return;
+    }
+  }
+  if (g && !graph_live) {
+    g->defer_free(ptr);  // captured kernels still read it on every replay
+    return;
+  }
+  if (lmpb_free(ptr, g_stream) != LMPB_OK) cudaGetLastError();  // no stale error for the next launch check
 }
 
 Storage make_storage(size_t bytes, DeviceType device) {
@@ -69,6 +90,7 @@ Storage make_storage(size_t bytes, DeviceType device) {
   s->device = device;
   if (bytes == 0) return s;
   if (device == DeviceType::CUDA) {
+    if (Graph* g = capturing_graph()) s->graph_live = g->live();
     LMPB_OK_OR_THROW(lmpb_malloc(&s->ptr, bytes, g_stream));
   } else {
     s->ptr = std::aligned_alloc(64, (bytes + 63) / 64 * 64);
@@ -276,6 +298,94 @@ void Tensor::fill(Scalar item) {
 }
 
 void Tensor::realize() { impl_->data(); }
+
+// ------------------------------------------------------- CUDA graphs
+
+namespace {
+thread_local Graph* t_graph = nullptr;
+
+void graph_check(cudaError_t e, const char* what) {
+  LMP_CHECK(e == cudaSuccess, "CUDA graph " << what << ": " << cudaGetErrorString(e));
+}
+}  // namespace
+
+Graph* capturing_graph() { return t_graph; }
+
+void Graph::capture_begin() {
+  LMP_CHECK(!t_graph, "a CUDA graph is already capturing on this thread");
+  LMP_CHECK(!exec_, "this Graph already holds a captured step");
+  cudaStream_t s = nullptr;
+  graph_check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream");
+  stream_ = s;
+  prev_ = g_stream;
+  // the capture starts after everything already queued on the host layer's stream
+  cudaEvent_t ev = nullptr;
+  graph_check(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming), "event");
+  graph_check(cudaEventRecord(ev, static_cast<cudaStream_t>(prev_)), "event record");
+  graph_check(cudaStreamWaitEvent(s, ev, 0), "stream wait");
+  cudaEventDestroy(ev);
+  graph_check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+  live_ = std::make_shared<bool>(true);
+  g_stream = s;
+  t_graph = this;
+  capturing_ = true;
+}
+
+void Graph::capture_abort() {
+  if (!capturing_) return;
+  *live_ = false;
+  cudaGraph_t g = nullptr;
+  cudaStreamEndCapture(static_cast<cudaStream_t>(stream_), &g);
+  if (g) cudaGraphDestroy(g);
+  cudaGetLastError();
+  g_stream = prev_;
+  t_graph = nullptr;
+  capturing_ = false;
+}
+
+void Graph::capture_end() {
+  LMP_CHECK(capturing_ && t_graph == this, "capture_end without capture_begin");
+  cudaGraph_t g = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(static_cast<cudaStream_t>(stream_), &g);
+  g_stream = prev_;
+  t_graph = nullptr;
+  capturing_ = false;
+  if (e != cudaSuccess || !g) {
+    *live_ = false;
+    cudaGetLastError();
+    LMP_CHECK(false, "CUDA graph capture failed (" << cudaGetErrorString(e)
+                                                   << "): the step read a value on the host or used an "
+                                                      "operation that cannot be captured");
+  }
+  graph_ = g;
+  size_t n = 0;
+  graph_check(cudaGraphGetNodes(g, nullptr, &n), "nodes");
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n) graph_check(cudaGraphGetNodes(g, nodes.data(), &n), "nodes");
+  kernels_ = 0;
+  for (auto& nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels_;
+  }
+  cudaGraphExec_t x = nullptr;
+  graph_check(cudaGraphInstantiateWithFlags(&x, g, cudaGraphInstantiateFlagAutoFreeOnLaunch), "instantiate");
+  exec_ = x;
+}
+
+void Graph::replay() {
+  LMP_CHECK(exec_, "replay before a completed capture");
+  LMP_CHECK(!t_graph, "replay while a CUDA graph is capturing");
+  graph_check(cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec_), static_cast<cudaStream_t>(g_stream)), "launch");
+}
+
+Graph::~Graph() {
+  if (capturing_ && t_graph == this) capture_abort();
+  cudaStream_t s = static_cast<cudaStream_t>(prev_);
+  if (exec_) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec_));
+  if (graph_) cudaGraphDestroy(static_cast<cudaGraph_t>(graph_));
+  for (void* p : deferred_) cudaFreeAsync(p, s);  // after the last replay on that stream
+  if (stream_) cudaStreamDestroy(static_cast<cudaStream_t>(stream_));
+}
 
 // ---------------------------------------------------- asynchronous host I/O
 
