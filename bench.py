@@ -229,17 +229,23 @@ def _backlog(torch, ms=20.0):
 
 
 def _time(torch, fn, iters, warmup=3):
+    """Median device time of one call of fn (ms): an event after every call,
+    launches queued behind a sleep kernel.  The median keeps a host hiccup
+    (these hosts are shared) from showing up as device time; the mean is
+    recorded beside it in `_time.last_mean`."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    e0, e1 = _events(torch)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
     _backlog(torch)
-    e0.record()
-    for _ in range(iters):
+    evs[0].record()
+    for i in range(iters):
         fn()
-    e1.record()
+        evs[i + 1].record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / iters
+    d = [evs[i].elapsed_time(evs[i + 1]) for i in range(iters)]
+    _time.last_mean = float(np.mean(d))
+    return float(np.median(d))
 
 
 def workload_c3(rsl, torch, args, rank=0, world=1):
@@ -310,9 +316,11 @@ def workload_c4(rsl, torch, args):
         B = rsl.Variable((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32), requires_grad=True)
         it = max(2, min(args.steps, int(2e13 / (m * n * k))))
         fwd = _time(torch, lambda: rsl.matmul(A, B).realize(), it)
+        fwd_mean = _time.last_mean
         step = _time(torch, lambda: rsl.matmul(A, B).backward(), it)
         out[f"{m}x{k}x{n}"] = {"fwd_ms": fwd, "fwd_TFLOPs": 2 * m * n * k / fwd / 1e9,
-                               "fwd_bwd_ms": step, "fwd_bwd_TFLOPs": 6 * m * n * k / step / 1e9}
+                               "fwd_bwd_ms": step, "fwd_bwd_TFLOPs": 6 * m * n * k / step / 1e9,
+                               "mean_ms": {"fwd": fwd_mean, "fwd_bwd": _time.last_mean}}
         tot_f += 6 * m * n * k
         tot_ms += step
     try:
@@ -322,6 +330,7 @@ def workload_c4(rsl, torch, args):
     peak = bf16 / 3  # fp16 issues at the bf16 rate; three MMAs per fp32 product
     value = tot_f / tot_ms / 1e9
     return {"metric": "fp32 matmul TFLOP/s, fwd + dA + dB (C4 sweep)", "value": value, "unit": "TFLOP/s",
+            "timing": "median of per-call CUDA-event times per shape (mean beside it)",
             "higher_is_better": True, "dtype": "f32 (scaled fp16 hi/lo split, 3 MMAs, on tcgen05)",
             "config": {"workload": "C4 matmul sweep"}, "shapes": out,
             "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s",

@@ -237,7 +237,11 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
   p.vec = 1;
   for (int v = want; v > 1; v >>= 1)
     if (inner % v == 0) { p.vec = v; break; }
-  if (p.pattern == kRowReduce) p.warp_rows = inner < 2048;
+  if (p.pattern == kRowReduce) {
+    int64_t warp_max = 2048;  // rows shorter than this get a warp each, longer ones a CTA
+    if (const char* e = getenv("LMPB_FUSED_WARP_ROWS")) warp_max = atoll(e);  // tuning override
+    p.warp_rows = inner < warp_max;
+  }
   if (p.pattern == kColReduce) {
     const int64_t Q = p.size[1], P = p.size[0];
     const int64_t colblocks = (Q / p.vec + kThreads - 1) / kThreads;

@@ -418,11 +418,6 @@ __device__ __forceinline__ void drain_tile(uint32_t taddr, int row, int n0, int 
       const int col = min(n0 + c + j, N - 1);
       r[j] = __float_as_uint(pow2_scale(__uint_as_float(r[j]), -(erow + __ldg(eB + col))));
     }
-    if (ep.bias || ep.clamp) {  // beta is 0 whenever an epilogue is given
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        r[j] = __float_as_uint(epilogue_apply(ep, __uint_as_float(r[j]), min(n0 + c + j, N - 1)));
-    }
     if (vec && ncols == 16) {
 #pragma unroll
       for (int j = 0; j < 16; j += 4) {
@@ -435,13 +430,20 @@ __device__ __forceinline__ void drain_tile(uint32_t taddr, int row, int n0, int 
           v.z = __fadd_rn(o.z, v.z);
           v.w = __fadd_rn(o.w, v.w);
         }
+        if (ep.bias || ep.clamp) {
+          const int col = n0 + c + j;
+          v.x = epilogue_apply(ep, v.x, col);
+          v.y = epilogue_apply(ep, v.y, col + 1);
+          v.z = epilogue_apply(ep, v.z, col + 2);
+          v.w = epilogue_apply(ep, v.w, col + 3);
+        }
         *reinterpret_cast<float4*>(crow + j) = v;
       }
     } else {
       for (int j = 0; j < ncols; ++j) {
         float v = __uint_as_float(r[j]);
         if (beta) v = __fadd_rn(crow[j], v);
-        crow[j] = v;
+        crow[j] = epilogue_apply(ep, v, n0 + c + j);
       }
     }
   }
@@ -634,11 +636,46 @@ __host__ __device__ constexpr uint32_t instr_desc_pair() {
   return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(P_TM >> 4) << 24);
 }
 
+// Four adjacent outputs of one row (columns col..col+3 at dst): unscale by
+// 2^-(e_row+e_col), + C when beta, then the epilogue's bias and clamp.
+__device__ __forceinline__ void store_quad(float* dst, int col, int N, bool vec, int erow, const int* __restrict__ eB,
+                                           float4 v, int beta, const Epilogue& ep) {
+  if (vec && col + 3 < N) {
+    const int4 ec = __ldg(reinterpret_cast<const int4*>(eB + col));
+    float4 o = make_float4(pow2_scale(v.x, -(erow + ec.x)), pow2_scale(v.y, -(erow + ec.y)),
+                           pow2_scale(v.z, -(erow + ec.z)), pow2_scale(v.w, -(erow + ec.w)));
+    if (beta) {
+      const float4 p = *reinterpret_cast<const float4*>(dst);
+      o.x = __fadd_rn(p.x, o.x);
+      o.y = __fadd_rn(p.y, o.y);
+      o.z = __fadd_rn(p.z, o.z);
+      o.w = __fadd_rn(p.w, o.w);
+    }
+    if (ep.bias || ep.clamp) {
+      o.x = epilogue_apply(ep, o.x, col);
+      o.y = epilogue_apply(ep, o.y, col + 1);
+      o.z = epilogue_apply(ep, o.z, col + 2);
+      o.w = epilogue_apply(ep, o.w, col + 3);
+    }
+    *reinterpret_cast<float4*>(dst) = o;
+  } else {
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (col + i < N) {
+        float o = pow2_scale(vv[i], -(erow + __ldg(eB + col + i)));
+        if (beta) o = __fadd_rn(dst[i], o);
+        dst[i] = epilogue_apply(ep, o, col + i);
+      }
+  }
+}
+
 __global__ void __launch_bounds__(kThreadsP, 1)
     gemm_f16x3_pair_kernel(const __grid_constant__ CUtensorMap tAh, const __grid_constant__ CUtensorMap tAl,
                            const __grid_constant__ CUtensorMap tBh, const __grid_constant__ CUtensorMap tBl,
                            const int* __restrict__ eA, const int* __restrict__ eB, float* __restrict__ C, int M,
-                           int N, int num_kb, int beta, int tiles_m, int tiles_n, Epilogue ep) {
+                           int N, int num_kb, int beta, int tiles_m, int tiles_n, Epilogue ep, int splits,
+                           float* __restrict__ part, unsigned* __restrict__ arrivals) {
   extern __shared__ uint8_t smem_raw[];
   // The same offsets in both CTAs: the pair MMA addresses the peer's tiles
   // and the commits address the peer's barriers by the local offset.
@@ -653,7 +690,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int num_tiles = tiles_m * tiles_n;
+  // Work units: tile t = u / splits covers k-blocks [ks * kb_per, ...) with
+  // ks = u % splits; with splits > 1 the unit that finishes a tile last sums
+  // the partials (see the epilogue).
+  const int num_units = tiles_m * tiles_n * splits;
+  const int kb_per = (num_kb + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -683,11 +724,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tBl)) : "memory");
     uint32_t it = 0;
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += npairs) {
+    for (int u = pair; u < num_units && ok; u += npairs) {
+      const int t = u / splits, kb0 = (u % splits) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
       int m0, n0;
       tile_coords_pair(t, tiles_m, tiles_n, m0, n0);
       const int ya = m0 + (int)rank * 128, yb = n0 + (int)rank * 128;
-      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % P_STAGES;
         const uint32_t phase = (it / P_STAGES) & 1;
         if (!mbar_wait(smem_u32(&empty[s]), phase ^ 1, 5)) {
@@ -710,11 +752,12 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     uint32_t it = 0;
     bool ok = true;
     int lt = 0;
-    for (int t = pair; t < num_tiles && ok; t += npairs, ++lt) {
+    for (int u = pair; u < num_units && ok; u += npairs, ++lt) {
+      const int kb0 = (u % splits) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
       if (!mbar_wait(smem_u32(&tempty[0]), (lt & 1) ^ 1, 6)) break;  // both epilogues drained
       tc_fence_after();
       const uint32_t dbig = tmem, dsmall = tmem + (uint32_t)BN;
-      for (int kb = 0; kb < num_kb; ++kb, ++it) {
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % P_STAGES;
         const uint32_t phase = (it / P_STAGES) & 1;
         if (!mbar_wait(smem_u32(&full[s]), phase, 7)) {
@@ -728,7 +771,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint64_t off = (uint64_t)((kk * 32) >> 4);
-          const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+          const uint32_t first = (kb == kb0 && kk == 0) ? 0u : 1u;
           mma_f16_pair(dsmall, dAl + off, dBh + off, idesc, first);
           mma_f16_pair(dsmall, dAh + off, dBl + off, idesc, 1u);
           mma_f16_pair(dbig, dAh + off, dBh + off, idesc, first);
@@ -748,7 +791,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     const uint32_t tempty_leader = map_to_cta(smem_u32(&tempty[0]), 0);
     const bool vec = (N & 3) == 0;
     int lt = 0;
-    for (int t = pair; t < num_tiles; t += npairs, ++lt) {
+    for (int u = pair; u < num_units; u += npairs, ++lt) {
+      const int t = u / splits, ks = u % splits;
       const bool ok = mbar_wait(smem_u32(&tfull[0]), lt & 1, 8);
       tc_fence_after();
       int m0, n0;
@@ -774,43 +818,50 @@ __global__ void __launch_bounds__(kThreadsP, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader);
-      if (ok && row < M) {
+      if (splits > 1) {
+        // Split-K: every unit leaves its 32 x 128 block of (pre-scale)
+        // partial sums in `part`; the unit whose arrival completes the
+        // count adds the splits' partials in split order and finishes, so
+        // the result does not depend on which unit came last.  No unit
+        // waits for another.
+        const int blk = (int)rank * 8 + (warp - 2);
+        const size_t bsz = 32 * 128;
+        float4* mine = reinterpret_cast<float4*>(part + ((size_t)u * 16 + blk) * bsz);
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) mine[(c >> 2) * 32 + lane] = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(arrivals + (size_t)t * 16 + blk, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev == (unsigned)(splits - 1) && ok && row < M) {
+          __threadfence();
+          const int erow = __ldg(eA + row);
+          const int c0 = n0 + h * 128;
+          float* crow = C + (int64_t)row * N + c0;
+          const float4* tp = reinterpret_cast<const float4*>(part + ((size_t)t * splits * 16 + blk) * bsz);
+#pragma unroll 4
+          for (int c = 0; c < 128; c += 4) {
+            float4 a = __ldcg(tp + (c >> 2) * 32 + lane);
+            for (int k = 1; k < splits; ++k) {
+              const float4 b = __ldcg(tp + (size_t)k * 16 * (bsz / 4) + (c >> 2) * 32 + lane);
+              a.x = __fadd_rn(a.x, b.x);
+              a.y = __fadd_rn(a.y, b.y);
+              a.z = __fadd_rn(a.z, b.z);
+              a.w = __fadd_rn(a.w, b.w);
+            }
+            store_quad(crow + c, c0 + c, N, vec, erow, eB, a, beta, ep);
+          }
+        }
+      } else if (ok && row < M) {
         const int erow = __ldg(eA + row);
         const int c0 = n0 + h * 128;
         float* crow = C + (int64_t)row * N + c0;
 #pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          const int col = c0 + c;
-          if (vec && col + 3 < N) {
-            const int4 ec = __ldg(reinterpret_cast<const int4*>(eB + col));
-            float4 o = make_float4(pow2_scale(v[c], -(erow + ec.x)), pow2_scale(v[c + 1], -(erow + ec.y)),
-                                   pow2_scale(v[c + 2], -(erow + ec.z)), pow2_scale(v[c + 3], -(erow + ec.w)));
-            if (ep.bias || ep.clamp) {
-              o.x = epilogue_apply(ep, o.x, col);
-              o.y = epilogue_apply(ep, o.y, col + 1);
-              o.z = epilogue_apply(ep, o.z, col + 2);
-              o.w = epilogue_apply(ep, o.w, col + 3);
-            }
-            if (beta) {
-              const float4 p = *reinterpret_cast<const float4*>(crow + c);
-              o.x = __fadd_rn(p.x, o.x);
-              o.y = __fadd_rn(p.y, o.y);
-              o.z = __fadd_rn(p.z, o.z);
-              o.w = __fadd_rn(p.w, o.w);
-            }
-            *reinterpret_cast<float4*>(crow + c) = o;
-          } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (col + i < N) {
-                float o = pow2_scale(v[c + i], -(erow + __ldg(eB + col + i)));
-                if (beta) o = __fadd_rn(crow[c + i], o);
-                o = epilogue_apply(ep, o, col + i);
-                crow[c + i] = o;
-              }
-          }
-        }
+        for (int c = 0; c < 128; c += 4)
+          store_quad(crow + c, c0 + c, N, vec, erow, eB, make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]), beta, ep);
       }
+      (void)ks;
       if (!ok) break;
     }
   }
@@ -968,6 +1019,7 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
     return v && v[0] == '0';
   }();
   const bool pair = m >= P_TM && !pair_off;
+  int splits = 1;  // split-K for the pair kernel, chosen below
   CUtensorMap mAh, mAl, mBh, mBl;
   const int b_box = pair ? BN / 2 : BN;
   if (s == LMPB_OK) s = make_map(&mAh, Ah, m, Kp, BM);
@@ -980,11 +1032,35 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   const int nkb = (int)(Kp / BK), bflag = beta != 0.f ? 1 : 0;
   if (s == LMPB_OK && pair) {
     int clusters = pair_clusters();
-    if (clusters <= 0) {
+    // Split K when it shortens the run: time ~ rounds(units) / splits with
+    // rounds = ceil(ntiles * splits / clusters); at least 8 k-blocks per split
+    // and a gain of 5 % to pay for the partial sums' traffic.
+    if (clusters > 0 && !getenv("LMPB_GEMM_NO_SPLITK")) {
+      auto cost = [&](int sp) { return (double)((ntiles * sp + clusters - 1) / clusters) / sp; };
+      double best = cost(1);
+      for (int sp = 2; sp <= 4 && nkb / sp >= 8; ++sp)
+        if (cost(sp) < best * 0.95) best = cost(sp), splits = sp;
+    }
+    void* sk = nullptr;
+    float* part = nullptr;
+    unsigned* arrivals = nullptr;
+    if (clusters > 0 && splits > 1) {
+      const size_t pbytes = (size_t)ntiles * splits * 16 * 32 * 128 * 4, abytes = (size_t)ntiles * 16 * 4;
+      cudaError_t ae = stream_alloc(&sk, pbytes + abytes, st);
+      if (ae == cudaSuccess) ae = cudaMemsetAsync(static_cast<char*>(sk) + pbytes, 0, abytes, st);
+      if (ae != cudaSuccess) {
+        s = set_error(LMPB_ERR_CUDA, std::string("gemm split-K workspace: ") + cudaGetErrorString(ae));
+      } else {
+        part = static_cast<float*>(sk);
+        arrivals = reinterpret_cast<unsigned*>(static_cast<char*>(sk) + pbytes);
+      }
+    }
+    if (s != LMPB_OK) {
+    } else if (clusters <= 0) {
       s = set_error(LMPB_ERR_CUDA, "gemm: no CTA-pair cluster fits on this device");
     } else {
       cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles, clusters)));
+      cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(ntiles * splits, clusters)));
       cfg.blockDim = dim3(kThreadsP);
       cfg.dynamicSmemBytes = P_SMEM_BYTES;
       cfg.stream = st;
@@ -997,10 +1073,11 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
       cfg.numAttrs = 1;
       const cudaError_t le = cudaLaunchKernelEx(&cfg, gemm_f16x3_pair_kernel, mAh, mAl, mBh, mBl, (const int*)exA,
                                                 (const int*)exB, C, (int)m, (int)n, nkb, bflag, (int)tiles_m,
-                                                (int)tiles_n, ep);
+                                                (int)tiles_n, ep, splits, part, arrivals);
       s = le != cudaSuccess ? set_error(LMPB_ERR_CUDA, std::string("gemm pair launch: ") + cudaGetErrorString(le))
                             : launch_status("gemm_f16x3_pair_kernel");
     }
+    if (sk) cudaFreeAsync(sk, st);
   } else if (s == LMPB_OK) {
     const unsigned grid = (unsigned)std::min<int64_t>(ntiles, sm_count());
     gemm_f16x3_kernel<<<grid, kThreads, SMEM_BYTES, st>>>(mAh, mAl, mBh, mBl, exA, exB, C, (int)m, (int)n, nkb, bflag,

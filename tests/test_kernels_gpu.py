@@ -374,3 +374,29 @@ def test_gemm_f32_c4_sizes(cuda, mkn, tol):
     capi.device_error()
     ref = A.double() @ B.double()
     assert ((C.double() - ref).abs().max() / ref.abs().max()).item() <= tol
+
+
+@pytest.mark.parametrize("mkn", [(4096, 1024, 4096), (8192, 4096, 1000), (4096, 8192, 4096)])
+def test_gemm_f32_split_k_deterministic(cuda, mkn, monkeypatch):
+    """Shapes with fewer tiles than CTA pairs split K; the last-arriving unit
+    sums the partials in split order, so repeated runs are bit-identical and
+    match the unsplit kernel within the GEMM tolerance, with accumulation
+    into C (beta = 1) too."""
+    torch = cuda
+    m, k, n = mkn
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    A = torch.randn(m, k, device="cuda", generator=g) / k ** 0.5
+    B = torch.randn(k, n, device="cuda", generator=g)
+    C0 = torch.randn(m, n, device="cuda", generator=g)
+    outs = []
+    for nosplit in (False, False, True):
+        if nosplit:
+            monkeypatch.setenv("LMPB_GEMM_NO_SPLITK", "1")
+        C = C0.clone()
+        capi.gemm_f32(0, 0, A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, 1.0)
+        capi.device_error()
+        outs.append(C)
+    assert torch.equal(outs[0], outs[1])
+    ref = A.double() @ B.double() + C0.double()
+    for C in outs:
+        assert ((C.double() - ref).abs().max() / ref.abs().max()).item() <= 1e-5
