@@ -1032,14 +1032,19 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   const int nkb = (int)(Kp / BK), bflag = beta != 0.f ? 1 : 0;
   if (s == LMPB_OK && pair) {
     int clusters = pair_clusters();
-    // Split K when it shortens the run: time ~ rounds(units) / splits with
-    // rounds = ceil(ntiles * splits / clusters); at least 8 k-blocks per split
-    // and a gain of 5 % to pay for the partial sums' traffic.
-    if (clusters > 0 && !getenv("LMPB_GEMM_NO_SPLITK")) {
+    // Split K in two when it shortens the run: time ~ rounds(units) / splits
+    // with rounds = ceil(ntiles * splits / clusters), a gain of 5 % required.
+    // Measured on B200, a split unit costs more than its share of the MMAs
+    // (4096^3: 2 splits 0.50 ms vs 0.46 ms unsplit, 4 splits 1.1 ms), so
+    // only long K (>= 256 k-blocks, K >= 8192) is split, and only in two
+    // (4096 x 8192 x 4096: 0.80 ms vs 0.84 ms; K = 32768: 2.8 ms vs 3.35 ms).
+    const char* force = getenv("LMPB_GEMM_SPLITK");  // tuning override: the split count (1 = none)
+    if (clusters > 0 && force) {
+      splits = std::max(1, std::min(atoi(force), std::max(1, nkb)));
+    } else if (clusters > 0) {
       auto cost = [&](int sp) { return (double)((ntiles * sp + clusters - 1) / clusters) / sp; };
       double best = cost(1);
-      for (int sp = 2; sp <= 4 && nkb / sp >= 8; ++sp)
-        if (cost(sp) < best * 0.95) best = cost(sp), splits = sp;
+      if (nkb >= 256 && cost(2) < best * 0.95) splits = 2;
     }
     void* sk = nullptr;
     float* part = nullptr;

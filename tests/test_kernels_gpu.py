@@ -376,12 +376,13 @@ def test_gemm_f32_c4_sizes(cuda, mkn, tol):
     assert ((C.double() - ref).abs().max() / ref.abs().max()).item() <= tol
 
 
-@pytest.mark.parametrize("mkn", [(4096, 1024, 4096), (8192, 4096, 1000), (4096, 8192, 4096)])
-def test_gemm_f32_split_k_deterministic(cuda, mkn, monkeypatch):
-    """Shapes with fewer tiles than CTA pairs split K; the last-arriving unit
-    sums the partials in split order, so repeated runs are bit-identical and
-    match the unsplit kernel within the GEMM tolerance, with accumulation
-    into C (beta = 1) too."""
+@pytest.mark.parametrize("mkn,splits", [((4096, 8192, 4096), None), ((4096, 1024, 4096), "2"),
+                                        ((8192, 4096, 1000), "3"), ((2048, 4096, 1000), "4")])
+def test_gemm_f32_split_k_deterministic(cuda, mkn, splits, monkeypatch):
+    """Split K (chosen by the heuristic when splits is None, else forced with
+    the tuning override): the last-arriving unit sums the partials in split
+    order, so repeated runs are bit-identical, and they match the unsplit
+    kernel within the GEMM tolerance, with accumulation into C (beta = 1)."""
     torch = cuda
     m, k, n = mkn
     g = torch.Generator(device="cuda").manual_seed(m + n)
@@ -389,9 +390,11 @@ def test_gemm_f32_split_k_deterministic(cuda, mkn, monkeypatch):
     B = torch.randn(k, n, device="cuda", generator=g)
     C0 = torch.randn(m, n, device="cuda", generator=g)
     outs = []
-    for nosplit in (False, False, True):
-        if nosplit:
-            monkeypatch.setenv("LMPB_GEMM_NO_SPLITK", "1")
+    for unsplit in (False, False, True):
+        if unsplit:
+            monkeypatch.setenv("LMPB_GEMM_SPLITK", "1")
+        elif splits:
+            monkeypatch.setenv("LMPB_GEMM_SPLITK", splits)
         C = C0.clone()
         capi.gemm_f32(0, 0, A.data_ptr(), B.data_ptr(), C.data_ptr(), m, n, k, 1.0)
         capi.device_error()
