@@ -68,8 +68,9 @@ def _ours_step(rsl, params, x, y, lr):
     return [q.numpy() for q in new], float(loss.numpy().ravel()[0])
 
 
-@pytest.mark.parametrize("dims,batch,steps", [([256, 64, 10], 32, 5), ([512, 512, 512, 100], 256, 3)],
-                         ids=["readme_mlp", "c5_narrow"])
+@pytest.mark.parametrize("dims,batch,steps", [([256, 64, 10], 32, 5), ([512, 512, 512, 100], 256, 3),
+                                               ([1024, 1024, 1024, 1000], 512, 2)],
+                         ids=["readme_mlp", "c5_narrow", "c5_wide_head"])
 def test_mlp_training_matches_reference(cuda, dims, batch, steps):
     import rushlite_b200 as rsl
 
