@@ -47,6 +47,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 #include <string>
 
 #include "common.cuh"
@@ -979,15 +980,23 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
     if (s == LMPB_OK && clamp) s = lmpb_unary(LMPB_CLAMP, LMPB_FLOAT32, C, C, m * n, lo, hi, st);
     return s;
   }
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_f16x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      P_SMEM_BYTES);
-  });
-  if (attr_err != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(attr_err));
+  // The shared-memory opt-in is per device: set it the first time each
+  // device (the current one) runs the tensor-core path.
+  {
+    static std::mutex mu;
+    static std::vector<char> ready;
+    int dev = 0;
+    LMPB_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)ready.size() <= dev) ready.resize(dev + 1, 0);
+    if (!ready[dev]) {
+      cudaError_t ae = cudaFuncSetAttribute(gemm_f16x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      if (ae == cudaSuccess)
+        ae = cudaFuncSetAttribute(gemm_f16x3_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+      if (ae != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(ae));
+      ready[dev] = 1;
+    }
+  }
   const int64_t Kp = (k + BK - 1) / BK * BK;
   auto up = [](size_t b) { return (b + 255) / 256 * 256; };
   const size_t plane_a = up((size_t)m * Kp * 2), plane_b = up((size_t)n * Kp * 2);
