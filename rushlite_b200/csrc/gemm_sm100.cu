@@ -349,6 +349,46 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// split_transpose_kernel with 16-byte traffic both ways (rows % 4 == 0, src
+// 16-byte aligned): the 64 x 64 tile is filled by float4 loads along the
+// rows, and each thread writes 8 adjacent k (16 bytes) of one output row.
+__global__ void __launch_bounds__(256)
+    split_transpose4_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp,
+                            const float* __restrict__ colmax, __half* __restrict__ hi, __half* __restrict__ lo,
+                            int* __restrict__ expo) {
+  __shared__ float tile[64][65];
+  const int64_t k0 = (int64_t)blockIdx.y * 64, r0 = (int64_t)blockIdx.x * 64;
+  {
+    const int tq = threadIdx.x & 15, tk = threadIdx.x >> 4;  // 16 column-quads x 16 k
+#pragma unroll
+    for (int j = tk; j < 64; j += 16) {
+      const int64_t k = k0 + j, r = r0 + 4 * tq;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < K && r < rows) v = __ldg(reinterpret_cast<const float4*>(src + k * rows + r));
+      tile[j][4 * tq] = v.x;
+      tile[j][4 * tq + 1] = v.y;
+      tile[j][4 * tq + 2] = v.z;
+      tile[j][4 * tq + 3] = v.w;
+    }
+  }
+  __syncthreads();
+  const int kg = threadIdx.x & 7, ry = threadIdx.x >> 3;  // 8 groups of 8 k x 32 rows
+  const int64_t k = k0 + 8 * kg;
+#pragma unroll
+  for (int j = ry; j < 64; j += 32) {
+    const int64_t r = r0 + j;
+    if (r < rows && k < Kp) {  // Kp is a multiple of 32, so all 8 are inside
+      const int e = row_exp(__ldg(colmax + r));
+      if (blockIdx.y == 0 && kg == 0) expo[r] = e;  // once per row
+      __half h[8], l[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) split16(pow2_scale(tile[8 * kg + i][j], e), h[i], l[i]);
+      *reinterpret_cast<uint4*>(hi + r * Kp + k) = *reinterpret_cast<const uint4*>(h);
+      *reinterpret_cast<uint4*>(lo + r * Kp + k) = *reinterpret_cast<const uint4*>(l);
+    }
+  }
+}
+
 // ------------------------------------------------------------ GEMM kernel
 
 // Tile t of a tiles_m x tiles_n grid in grouped order: 8 row-tiles at a time
@@ -952,12 +992,16 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
   }
   if ((Kp + 63) / 64 > 65535 || (K + 255) / 256 > 65535)
     return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
+  const bool quad = (rows & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
   colmax_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + 255) / 256)), 256, 0, st>>>(
       src, rows, K, reinterpret_cast<unsigned*>(rowmax));
   lmpb_status s = launch_status("gemm split pass (column maxima)");
   if (s != LMPB_OK) return s;
-  split_transpose_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64)), 256, 0, st>>>(
-      src, rows, K, Kp, rowmax, hi, lo, expo);
+  const dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64));
+  if (quad)
+    split_transpose4_kernel<<<grid, 256, 0, st>>>(src, rows, K, Kp, rowmax, hi, lo, expo);
+  else
+    split_transpose_kernel<<<grid, 256, 0, st>>>(src, rows, K, Kp, rowmax, hi, lo, expo);
   return launch_status("gemm split pass (transpose)");
 }
 
