@@ -709,9 +709,9 @@ def main():
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_src,
                      # dram__bytes_read.sum + dram__bytes_write.sum of the backward kernel from
-                     # the ncu capture in profiles/fused_c2_backward_ncu_full.md (4096 rows:
-                     # 268.5 MB + 92.3 MB), scaled by the rows to this launch; the rest of
-                     # grad_a's writes are still dirty in L2 when the kernel ends
+                     # one ncu capture at 4096 rows (268.5 MB + 92.3 MB), scaled by the rows to
+                     # this launch; the rest of grad_a's writes are still dirty in L2 when the
+                     # kernel ends
                      "traffic": (268.5e6 + 92.3e6) * ROWS / 4096 if ROWS >= 4096 else None,
                      "traffic_source": "ncu capture at 4096 rows, scaled by rows per launch",
                      "forward_achieved": FWD_BYTES / (fwd_ms / 1e3) / 1e9},

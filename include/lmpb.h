@@ -15,7 +15,7 @@
  * per op and device in a `DispatchStub` table
  * (csrc/include/lamp3/tensor/dispatch_stub.hpp:21-64); a CUDA registration
  * unit built on this header wraps each stub signature around one call here
- * (the shim is shown in INTEGRATION.md).
+ * (allocate the output, call the lmpb_* function, throw on a non-OK status).
  *
  * Errors: every call returns an lmpb_status.  LMPB_ERR_INVALID mirrors the
  * reference's user-error LMP_CHECK (a throw of std::runtime_error,
