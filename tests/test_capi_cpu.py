@@ -48,8 +48,13 @@ def test_invalid_arguments_are_reported_without_a_gpu():
     assert L.lmpb_unary(0, 17, None, None, 4, 0.0, 0.0, None) == 1
     assert L.lmpb_reduce(0, 4, None, capi.shape_arr([3]), 1, 2, None, None) == 1
     assert L.lmpb_gemm_f32(0, 0, None, None, None, 2, 2, 2, C.c_float(0.5), None) == 1
+    # the fused Linear entry: negative sizes and missing pointers are user errors
+    assert L.lmpb_gemm_f32_bias_act(0, 0, None, None, None, -1, 2, 2, None, 0, 0.0, 0.0, None) == 1
+    assert L.lmpb_gemm_f32_bias_act(0, 0, None, None, None, 2, 2, 2, None, 1, 0.0, 1.0, None) == 1
+    assert b"lmpb_gemm_f32_bias_act" in L.lmpb_last_error()
     # zero-size work is a no-op
     assert L.lmpb_unary(0, 4, None, None, 0, 0.0, 0.0, None) == 0
+    assert L.lmpb_gemm_f32_bias_act(0, 0, None, None, None, 0, 8, 8, None, 1, 0.0, 1.0, None) == 0
 
 
 def _nvrtc():
