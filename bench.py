@@ -446,9 +446,9 @@ def _mlp_step_inplace(rsl, ps, x, y, lr):
         p = e / rsl.sum(e, 1)
     loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
     loss.backward()
-    with rsl.no_grad():
+    with rsl.no_grad(), rsl.capture_on():
         for q in ps:
-            q.data.copy(q.data - lr * q.grad)
+            q.data.copy(q.data - lr * q.grad)  # one fused kernel, written in place
             q.zero_grad()
     return loss
 

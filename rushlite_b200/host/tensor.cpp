@@ -269,8 +269,39 @@ Tensor Tensor::to(DeviceType device) const {
   return Tensor(out);
 }
 
+// True when realizing `t` straight into storage `dst` (of shape `shape`) is
+// safe: every read of dst in the expression is at the index being written
+// (same shape, no broadcast) and dst carries no pending value of its own.
+static bool in_place_safe(const TensorImpl* t, const StorageImpl* dst, const std::vector<size_t>& shape,
+                          std::unordered_set<const TensorImpl*>& seen) {
+  if (!seen.insert(t).second) return true;
+  if (t->storage.get() == dst) return !t->lazy && t->shape == shape;
+  if (!t->lazy) return true;
+  for (const auto& in : t->lazy->inputs)
+    if (!in_place_safe(in.get(), dst, shape, seen)) return false;
+  return true;
+}
+
 void Tensor::copy(const Tensor& other) {
   LMP_CHECK(other.numel() == numel(), "copy: size mismatch");
+  const ImplPtr& o = other.impl();
+  if (device() == DeviceType::CUDA && other.device() == DeviceType::CUDA && o->lazy && !impl_->lazy &&
+      impl_->storage && other.type() == type() && other.shape() == shape() &&
+      (o->lazy->kind == LazyNode::kBinary || o->lazy->kind == LazyNode::kUnary)) {
+    std::unordered_set<const TensorImpl*> seen;
+    if (in_place_safe(o.get(), impl_->storage.get(), shape(), seen)) {
+      // one fused kernel writes the pending elementwise value into this
+      // storage (e.g. an in-place SGD update p.copy(p - lr * g))
+      auto t = std::make_shared<TensorImpl>();
+      t->shape = shape();
+      t->dtype = type();
+      t->device = DeviceType::CUDA;
+      t->storage = impl_->storage;
+      t->lazy = o->lazy;
+      realize_all({t});
+      return;
+    }
+  }
   void* dst = impl_->data();
   const void* src = other.impl()->data();
   const size_t n = numel();

@@ -43,9 +43,9 @@ def _step_inplace(rsl, ps, x, y, lr):
         p = e / rsl.sum(e, 1)
     loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
     loss.backward()
-    with rsl.no_grad():
+    with rsl.no_grad(), rsl.capture_on():
         for q in ps:
-            q.data.copy(q.data - lr * q.grad)
+            q.data.copy(q.data - lr * q.grad)  # one fused kernel, written in place
             q.zero_grad()
     return loss
 
@@ -90,3 +90,21 @@ def test_host_read_inside_capture_fails_cleanly(rsl):
             (x * 2.0).numpy()  # a synchronising read cannot be recorded
     # the library keeps working on its own stream afterwards
     np.testing.assert_array_equal((x * 3.0).numpy(), np.full((64, 64), 3.0, np.float32))
+
+
+def test_copy_of_pending_value_writes_in_place(rsl):
+    """Tensor.copy of a pending elementwise value realizes it straight into
+    the destination (reading the destination's own old values at the same
+    index), with the same values as the unfused path."""
+    rng = np.random.default_rng(2)
+    a0 = rng.standard_normal((300, 257)).astype(np.float32)
+    g0 = rng.standard_normal((300, 257)).astype(np.float32)
+    r0 = rng.standard_normal((257,)).astype(np.float32)
+    got = []
+    for captured in (False, True):
+        a, g, r = rsl.Variable(a0), rsl.Variable(g0), rsl.Variable(r0)
+        with rsl.no_grad(), rsl.capture_on(captured):
+            a.data.copy(a.data - 1e-3 * g.data + r.data)  # broadcast of another tensor
+            a.data.copy(a.data * a.data + a.data)
+        got.append(a.numpy())
+    np.testing.assert_array_equal(got[0], got[1])
