@@ -101,6 +101,7 @@ struct Plan {
   bool idx32 = true;
   int64_t S = 1;                   // column-reduce row chunks
   bool warp_rows = false;          // row-reduce: warp per row
+  int row_unroll = 1;              // row-reduce: unroll factor of the walk along a row
 };
 
 }  // namespace
@@ -241,6 +242,7 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
     int64_t warp_max = 2048;  // rows shorter than this get a warp each, longer ones a CTA
     if (const char* e = getenv("LMPB_FUSED_WARP_ROWS")) warp_max = atoll(e);  // tuning override
     p.warp_rows = inner < warp_max;
+    if (const char* e = getenv("LMPB_FUSED_ROW_UNROLL")) p.row_unroll = std::max(1, atoi(e));  // tuning override
   }
   if (p.pattern == kColReduce) {
     const int64_t Q = p.size[1], P = p.size[0];
@@ -432,6 +434,7 @@ struct Gen {
     for (size_t j = 0; j < h.outs.size(); ++j)
       if (p.out_mode[j] >= LMPB_OUT_REDUCE_SUM)
         os << "    " << tname(h.outs[j].dtype) << " acc" << j << " = 0;\n";
+    if (p.row_unroll > 1) os << "    #pragma unroll " << p.row_unroll << "\n";
     os << "    for (" << I << " q = t * " << vec << "u; q < " << Q << "u; q += " << tpr << " * " << vec << "u) {\n";
     for (int m = 0; m < (int)h.nodes.size(); ++m)
       if (!done[m]) emit_node(m, "  ", loff);
