@@ -23,22 +23,31 @@
 //    contiguous, K padded to the k-block), transposing when the caller's
 //    layout is not K-major.  It reads each input element twice (the second
 //    read mostly from L2) and writes 4 bytes.
-// 2. The GEMM kernel: persistent, one CTA per SM walking 128 x BN output
-//    tiles in grouped order, 6 warps:
+// 2. The GEMM kernels.  For m >= 256 the CTA-pair kernel: 2-CTA clusters,
+//    persistent, each pair walking 256 x BN output tiles in grouped order
+//    with tcgen05.mma.cta_group::2 (M = 256); each CTA loads its own 128
+//    rows of A and 128 rows (half) of B per k-block, so B is loaded once per
+//    pair.  10 warps per CTA:
 //      warp 0     TMA producer (one elected thread): 4 tiles per k-block
-//                 (A hi/lo, B hi/lo) into a STAGES-deep shared-memory ring,
-//                 64-byte swizzled, completion on an mbarrier;
+//                 (A hi/lo, B hi/lo) into a 6-deep shared-memory ring,
+//                 64-byte swizzled; the bytes of both CTAs complete on the
+//                 leader CTA's mbarrier;
 //      warp 1     owns two TMEM accumulators (128 lanes x BN fp32 columns
-//                 each: hi*hi and the cross terms) and
-//                 issues the tcgen05.mma.kind::f16 instructions (one thread),
-//                 3 products x BK/16 MMAs per k-block, then tcgen05.commit
-//                 frees the stage;
-//      warps 2-5  epilogue: tcgen05.ld 32x32b from TMEM (each warp reads the
-//                 32 lanes its rank in the warpgroup may access), combine and
-//                 unscale, optional + C, 16-byte stores.
+//                 each: hi*hi and the cross terms); in the leader CTA one
+//                 thread issues 3 products x BK/16 MMAs per k-block, then a
+//                 tcgen05.commit that frees the stage in both CTAs;
+//      warps 2-9  epilogue: two warps per TMEM lane quarter, one per
+//                 128-column half, pull their combined values into registers
+//                 and release the accumulators, then unscale, add C, apply
+//                 the optional bias/clamp and store (overlapping the next
+//                 tile's MMAs).  Long K may be split in two; see the split-K
+//                 note in the pair kernel.
+//    For 64 <= m < 256 a single-CTA kernel with 128 x BN tiles (6 warps:
+//    producer, MMA issuer, 4 epilogue warps) does the same per tile.
 //    Every mbarrier wait is bounded (clock64); on expiry the kernel records
 //    an error code in a device word, stops issuing, frees TMEM and returns.
-//    No cluster launch and no multicast: each CTA loads its own tiles.
+//    No TMA load is multicast: each CTA loads its own tiles; only the
+//    commit's mbarrier arrival is multicast to the pair.
 // Shapes that TMA cannot describe or that are too small for a 128-row tile
 // use the SIMT kernel (gemm_simt.cu).
 #include <cuda.h>
