@@ -145,3 +145,18 @@ def test_fastdiv_emulation():
         for n in [0, 1, d - 1, d, d + 1, (1 << 31) - 1] + [rnd.randint(0, (1 << 31) - 1) for _ in range(200)]:
             t = (n * mul) >> 32
             assert ((t + n) >> s) == n // d, (n, d)
+
+
+@pytest.mark.parametrize("env,expect", [({"LMPB_FUSED_ROW_UNROLL": "4"}, "#pragma unroll 4"),
+                                        ({"LMPB_FUSED_WARP_ROWS": "100000"}, "wid; row <"),
+                                        ({"LMPB_FUSED_VEC_RED": "4"}, "Pack<float, 4>")])
+def test_fused_tuning_overrides_generate_and_compile(monkeypatch, env, expect):
+    """The tuning switches of the generated row-reduce kernel (unroll, warp
+    per row, packet width) change the source as documented and still compile."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    big = (64, 4096)  # rows of 4096: a CTA per row by default
+    f = capi.Fused(CHAIN, [(F32, big), (F32, (64, 1))],
+                   [(9, capi.OUT_STORE, F32, big), (5, capi.OUT_REDUCE_SUM, F32, (64, 1))], big)
+    assert expect in f.source
+    _compile(f.source)
