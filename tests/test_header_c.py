@@ -49,3 +49,21 @@ def test_header_compiles_as_cpp(tmp_path):
     src.write_text(PROGRAM)
     subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
                     str(src)], check=True)
+
+
+@pytest.mark.skipif(shutil.which("g++") is None, reason="g++ absent")
+def test_host_api_header_is_self_contained(tmp_path):
+    """The C++ Lamp3 API of this backend (lmp::tensor, lmp::autograd) compiles
+    from its one header plus the C ABI."""
+    src = tmp_path / "user.cpp"
+    src.write_text('#include "lamp.hpp"\n'
+                   "int main() {\n"
+                   "  using namespace lmp;\n"
+                   "  autograd::Variable (*mm)(const autograd::Variable&, const autograd::Variable&) =\n"
+                   "      &autograd::ops::matmul;\n"
+                   "  tensor::Graph* g = tensor::capturing_graph();\n"
+                   "  return (mm != nullptr && g == nullptr) ? 0 : 1;\n"
+                   "}\n")
+    cuda_inc = "/usr/local/cuda/include"
+    subprocess.run(["g++", "-std=c++17", "-Wall", "-Werror", "-fsyntax-only", "-I", os.path.join(ROOT, "include"),
+                    "-I", os.path.join(ROOT, "rushlite_b200", "host"), "-I", cuda_inc, str(src)], check=True)
