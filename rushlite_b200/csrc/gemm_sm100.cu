@@ -1103,6 +1103,9 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
     const char* force = getenv("LMPB_GEMM_SPLITK");  // tuning override: the split count (1 = none)
     if (clusters > 0 && force) {
       splits = std::max(1, std::min(atoi(force), std::max(1, nkb)));
+      // every unit needs at least one k-block: with kb_per = ceil(nkb / splits)
+      // the last unit starts at (splits - 1) * kb_per, which must be < nkb
+      while (splits > 1 && (splits - 1) * ((nkb + splits - 1) / splits) >= nkb) --splits;
     } else if (clusters > 0) {
       auto cost = [&](int sp) { return (double)((ntiles * sp + clusters - 1) / clusters) / sp; };
       double best = cost(1);
