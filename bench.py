@@ -148,7 +148,9 @@ def cpu_kind():
 
 
 def cpu_port_step(a, b):
-    """The C restatement (oracle/port) of the same forward + closed-form backward."""
+    """The C restatement (oracle/port) of the same forward and backward:
+    d = exp(c)*a - log(b+1) with c = a*a + b;
+    grad_a = exp(c)*(2a^2 + 1);  grad_b = rowsum(exp(c)*a) - cols/(b+1)."""
     from oracle import port
 
     t0 = time.perf_counter()
@@ -156,15 +158,30 @@ def cpu_port_step(a, b):
     s = port.binary(2, a, a)
     c = port.binary(0, s, b)
     x = port.unary(1, c)
-    d = port.binary(1, port.binary(2, x, a), port.unary(2, port.binary(0, b, one)))
-    ga = port.binary(0, port.binary(2, x, port.binary(2, a, a)), x)
-    gb = port.reduce(0, port.binary(2, x, a), 1)
+    b1 = port.binary(0, b, one)
+    d = port.binary(1, port.binary(2, x, a), port.unary(2, b1))
+    two_a2 = port.binary(2, s, np.full((1,), 2, np.float32))
+    ga = port.binary(2, x, port.binary(0, two_a2, one))
+    cols = np.full((1,), a.shape[1], np.float32)
+    gb = port.binary(1, port.reduce(0, port.binary(2, x, a), 1), port.binary(3, cols, b1))
     del d, ga, gb
     return time.perf_counter() - t0
 
 
-def cpu_baseline(a, b, budget_s=20.0):
+def cpu_threads(kind: str) -> int:
+    """Thread count of the CPU baseline: every core of the process's affinity
+    mask for the reference build (OpenMP; set explicitly, since torchrun
+    exports OMP_NUM_THREADS=1 into each rank), 1 for the scalar C port."""
+    if kind != "reference":
+        return 1
+    from oracle import ref
+
+    return ref.set_threads()
+
+
+def cpu_baseline(a, b, budget_s=15.0):
     kind = cpu_kind()
+    cores = cpu_threads(kind)
     step = cpu_reference_step if kind == "reference" else cpu_port_step
     step(a, b)  # warm-up (page faults)
     times = []
@@ -172,8 +189,7 @@ def cpu_baseline(a, b, budget_s=20.0):
     while time.perf_counter() - t_start < budget_s and len(times) < 5:
         times.append(step(a, b))
     med = float(np.median(times))
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": STEP_BYTES / med / 1e9, "unit": "GB/s", "cores": cores if kind == "reference" else 1,
+    return {"value": STEP_BYTES / med / 1e9, "unit": "GB/s", "cores": cores,
             "kind": kind, "sample": f"{len(times)} full C2 steps (fwd+bwd, [8192,8192]) after 1 warm-up, median {med:.3f} s"}
 
 
@@ -186,6 +202,7 @@ def run_reference_arm(args, rank, world):
         return
     a, b = inputs(0)
     kind = cpu_kind()
+    cores = cpu_threads(kind)
     step = cpu_reference_step if kind == "reference" else cpu_port_step
     probe = 512
     step(a[:probe], b[:probe])
@@ -199,7 +216,6 @@ def run_reference_arm(args, rank, world):
     total = float(np.sum(times))
     bytes_per_step = STEP_BYTES * rows / ROWS
     value = bytes_per_step * args.steps / total / 1e9
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
@@ -501,6 +517,165 @@ def workload_c1(rsl, torch, args):
             "timing": "host clock from the first replay to the last loss read (synchronising)"}
 
 
+# --------------------------------------------------------------------------
+# CPU baselines of the secondary configs: the reference's CPU build
+# (oracle/_ref) on a bounded sample of each workload, on every host core.
+
+def _ref_or_none():
+    from oracle import ref
+
+    return ref if ref.available() else None
+
+
+def cpu_baseline_c3():
+    """All C3 reductions and both sum backwards once each on the reference build."""
+    ref = _ref_or_none()
+    if ref is None:
+        return {"value": None, "error": "reference CPU build (oracle/_ref) absent"}
+    cores = ref.set_threads()
+    R, C = 16384, 4096
+    rng = np.random.default_rng(3)
+    xf = rng.standard_normal((R, C), dtype=np.float32)
+    xi = rng.integers(-1000, 1001, (R, C)).astype(np.int32)
+    vf, vi = ref.Var.of(xf), ref.Var.of(xi)
+    ref.reduce(0, vf, 0)  # warm-up
+    tot_b, tot_s = 0, 0.0
+    for op, v in ((0, vf), (1, vf), (2, vf), (0, vi)):
+        for axis in (0, 1):
+            t0 = time.perf_counter()
+            ref.reduce(op, v, axis)
+            tot_s += time.perf_counter() - t0
+            tot_b += R * C * 4 + (C if axis == 0 else R) * 4
+    for axis in (0, 1):
+        vg = ref.Var.of(xf, True)
+        t0 = time.perf_counter()
+        ref.reduce(0, vg, axis).backward()
+        tot_s += time.perf_counter() - t0
+        tot_b += 2 * R * C * 4
+    return {"value": tot_b / tot_s / 1e9, "unit": "GB/s", "cores": cores, "kind": "reference",
+            "sample": "the full C3 workload once: 8 reductions + 2 sum backwards of [16384, 4096]"}
+
+
+def cpu_baseline_c4():
+    ref = _ref_or_none()
+    if ref is None:
+        return {"value": None, "error": "reference CPU build (oracle/_ref) absent"}
+    cores = ref.set_threads()
+    m = k = n = 1024
+    rng = np.random.default_rng(m + k + n)
+    a = (rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    A, B = ref.Var.of(a, True), ref.Var.of(b, True)
+    t0 = time.perf_counter()
+    ref.matmul(A, B).backward()
+    dt = time.perf_counter() - t0
+    return {"value": 6 * m * n * k / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "reference",
+            "sample": "one 1024^3 matmul forward + dA + dB (the sweep's smallest shape; 8192^3 would take ~10 min)"}
+
+
+def _ref_mlp_step(ref, params, x, y, lr):
+    import sys as _s
+
+    P = [ref.Var.of(p, True) for p in params]
+    h = ref.Var.of(x)
+    n = len(P) // 2
+    for i in range(n):
+        h = ref.binary(0, ref.matmul(h, P[2 * i]), P[2 * i + 1])
+        if i < n - 1:
+            h = ref.unary(8, h, 0.0, _s.float_info.max)
+    m = ref.reduce(1, h, 1)
+    e = ref.unary(1, ref.binary(1, h, m))
+    p = ref.binary(3, e, ref.reduce(0, e, 1))
+    t = ref.binary(2, ref.unary(0, ref.Var.of(y)), ref.unary(2, ref.binary(0, p, ref.Var.of(np.array([1e-3], np.float32)))))
+    loss = ref.reduce(0, ref.reduce(0, t, 1), 0)
+    loss.backward()
+    lr32 = np.float32(lr)
+    return [(q.numpy() - lr32 * q.grad()).astype(np.float32) for q in P]
+
+
+def cpu_baseline_c1(steps=200):
+    ref = _ref_or_none()
+    if ref is None:
+        return {"value": None, "error": "reference CPU build (oracle/_ref) absent"}
+    cores = ref.set_threads()
+    rng = np.random.default_rng(0)
+    xs = rng.random((32, 256), dtype=np.float32)
+    ys = rng.random((32, 10), dtype=np.float32)
+    prng = np.random.default_rng(5)
+    ps = []
+    for i, o in ((256, 64), (64, 10)):
+        ps += [(prng.standard_normal((i, o)) / np.sqrt(i)).astype(np.float32),
+               (prng.standard_normal((o,)) / np.sqrt(i)).astype(np.float32)]
+    ps = _ref_mlp_step(ref, ps, xs, ys, 1e-3)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ps = _ref_mlp_step(ref, ps, xs, ys, 1e-3)
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "steps/s", "cores": cores, "kind": "reference",
+            "sample": f"{steps} README MLP steps through the reference's autograd (host-side parameter update)"}
+
+
+def cpu_baseline_c5(rows=64):
+    """C5 is ~3.2 TFLOP per step: on the host that is tens of minutes.  The
+    sample is a [rows, 4096] x [4096, 4096] product (the step's dominant GEMM
+    shape) on the reference build, and steps/s is extrapolated by GEMM FLOPs."""
+    ref = _ref_or_none()
+    if ref is None:
+        return {"value": None, "error": "reference CPU build (oracle/_ref) absent"}
+    cores = ref.set_threads()
+    rng = np.random.default_rng(7)
+    a = rng.standard_normal((rows, 4096)).astype(np.float32)
+    w = (rng.standard_normal((4096, 4096)) / 64).astype(np.float32)
+    A, W = ref.Var.of(a), ref.Var.of(w)
+    t0 = time.perf_counter()
+    ref.matmul(A, W)
+    dt = time.perf_counter() - t0
+    gflops = 2 * rows * 4096 * 4096 / dt / 1e9
+    return {"value": gflops * 1e9 / 3.225e12, "unit": "steps/s", "cores": cores, "kind": "reference",
+            "extrapolated": True, "gemm_GFLOPs": gflops,
+            "sample": f"one [{rows},4096]x[4096,4096] matmul on the reference build, steps/s = its FLOP rate / 3.225 TFLOP per step"}
+
+
+def run_secondary(rsl, torch, args, rank, world, pg, local):
+    """The other BASELINE configs, each with its own clock record, roofline and
+    (at N = 1) CPU baseline.  At N > 1: C3 (row-sharded, the dim-0 partials
+    all-reduced) and C5 (data parallel, gradient all-reduce); C4 and C1 are
+    single-GPU configs."""
+    names = ["c3", "c4", "c5", "c1"] if world == 1 else ["c3", "c5"]
+    cpu = {"c3": cpu_baseline_c3, "c4": cpu_baseline_c4, "c5": cpu_baseline_c5, "c1": cpu_baseline_c1}
+    blocks = {}
+    for name in names:
+        clocks = Clocks(local)
+        clocks.start()
+        time.sleep(0.5)
+        args.timed_window = None
+        wall0 = time.time()
+        l0 = rsl.cuda.kernel_launches()
+        try:
+            if name == "c3":
+                blk = workload_c3(rsl, torch, args, rank, world)
+            elif name == "c5":
+                blk = workload_c5(rsl, torch, args, rank, world, pg)
+            elif name == "c4":
+                blk = workload_c4(rsl, torch, args)
+            else:
+                blk = workload_c1(rsl, torch, args)
+        except Exception as e:  # a secondary block must never sink the headline line
+            blk = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        blk["gpu_launches_total"] = int(rsl.cuda.kernel_launches() - l0)
+        wall1 = time.time()
+        if wall1 - wall0 < 1.0:
+            time.sleep(1.0 - (wall1 - wall0))
+        blk["clocks"] = clocks.stop(*(args.timed_window or (wall0, wall1)))
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                blk["cpu_baseline"] = cpu[name]()
+            except Exception as e:
+                blk["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        blocks[name] = blk
+    return blocks
+
+
 def max_over_ranks_ms(torch, pg, ms):
     t = torch.tensor([ms], device="cuda")
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -514,6 +689,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="headline (C2) only; by default the line also carries C3, C4, C5 and C1 blocks")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--batch", type=int, default=8192, help="C5 global batch (8192 = the config)")
     ap.add_argument("--rows", type=int, default=8192, help="rows of a (8192 = the C2 config; smaller for profiling)")
@@ -687,6 +864,12 @@ def main():
     np.testing.assert_array_equal(outs[(args.e2e_steps - 1) % 2][2].shape, (ROWS, 1))
     if pg:
         e2e_ms = max_over_ranks_ms(torch, pg, e2e_ms)
+    h2d_b = int(pin_a.nbytes + pin_b.nbytes)
+    d2h_b = int(sum(x.nbytes for x in outs[0]))
+    secondary = None
+    if not args.no_secondary:
+        del pin_a, pin_b, outs
+        secondary = run_secondary(rsl, torch, args, rank, world, pg, local)
 
     if rank != 0:
         if pg:
@@ -719,10 +902,12 @@ def main():
         "clocks": clk,
         "e2e": {"value": STEP_BYTES * world / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
                 "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": int(pin_a.nbytes + pin_b.nbytes),
-                "d2h_bytes_per_step": int(sum(x.nbytes for x in outs[0])),
+                "h2d_bytes_per_step": h2d_b,
+                "d2h_bytes_per_step": d2h_b,
                 "timing": "host clock, K pipelined steps, all downloads completed"},
     }
+    if secondary is not None:
+        line["secondary"] = secondary
     if not args.no_cpu_baseline and world == 1:
         try:
             line["cpu_baseline"] = cpu_baseline(a_np, b_np)

@@ -45,6 +45,8 @@ def lib():
         L.lref_matmul.restype = vp
         L.lref_transpose.argtypes = [vp]
         L.lref_transpose.restype = vp
+        L.lref_set_threads.argtypes = [i]
+        L.lref_get_threads.restype = i
         _lib = L
     return _lib
 
@@ -114,3 +116,20 @@ def matmul(a: Var, b: Var) -> Var:
 
 def transpose(a: Var) -> Var:
     return Var(lib().lref_transpose(a.h))
+
+
+def host_cores() -> int:
+    """Cores this process may run on (its CPU affinity), whatever
+    OMP_NUM_THREADS a launcher exported."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - non-Linux
+        return os.cpu_count() or 1
+
+
+def set_threads(n: int | None = None) -> int:
+    """Sets the reference build's OpenMP thread count (default: every core of
+    the affinity mask) and returns the count now in effect."""
+    n = n or host_cores()
+    lib().lref_set_threads(int(n))
+    return int(lib().lref_get_threads())

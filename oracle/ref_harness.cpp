@@ -10,6 +10,8 @@
 #include <type_traits>
 #include <vector>
 
+#include <omp.h>
+
 #include "lamp3/lamp3.hpp"
 
 using lmp::autograd::Variable;
@@ -137,5 +139,11 @@ void* lref_matmul(void* a, void* b) {
 void* lref_transpose(void* a) { return wrap(aops::transpose(*static_cast<Variable*>(a))); }
 
 void lref_backward(void* h) { static_cast<Variable*>(h)->backward(); }
+
+// OpenMP thread count of the reference's parallel loops.  A launcher such as
+// torchrun exports OMP_NUM_THREADS=1 into every rank; the CPU baseline sets
+// the count explicitly to the cores the process may run on.
+void lref_set_threads(int n) { omp_set_num_threads(n); }
+int lref_get_threads(void) { return omp_get_max_threads(); }
 
 }  // extern "C"
