@@ -35,6 +35,12 @@ void with_type(int dt, F&& f) {
   }
 }
 
+// Device of the tensors lref_tensor creates.  The CPU build of the reference
+// (_ref/liblamp3_ref.so) only has the CPU device; the harness linked with the
+// reference core whose CUDA device is served by lmpb
+// (_ref/liblamp3_cuda_harness.so) creates CUDA tensors after lref_set_device(1).
+DeviceType g_device = DeviceType::CPU;
+
 Variable* wrap(const Variable& v) { return new Variable(v); }
 Variable* wrap_t(const Tensor& t) { return new Variable(t, false); }
 
@@ -54,7 +60,7 @@ void* lref_tensor(int dt, const void* data, const int64_t* shape, int ndim, int 
     std::vector<H> v(n);
     const T* src = static_cast<const T*>(data);
     for (size_t i = 0; i < n; ++i) v[i] = static_cast<H>(src[i]);
-    Tensor t(v, sh, DeviceType::CPU, static_cast<DataType>(dt));
+    Tensor t(v, sh, g_device, static_cast<DataType>(dt));
     out = new Variable(t, requires_grad != 0);
   });
   return out;
@@ -145,5 +151,12 @@ void lref_backward(void* h) { static_cast<Variable*>(h)->backward(); }
 // the count explicitly to the cores the process may run on.
 void lref_set_threads(int n) { omp_set_num_threads(n); }
 int lref_get_threads(void) { return omp_get_max_threads(); }
+
+void lref_set_device(int cuda) { g_device = cuda ? DeviceType::CUDA : DeviceType::CPU; }
+int lref_device(void* h) { return (int)static_cast<Variable*>(h)->data().device(); }
+// The thread's capture flag (lmp::tensor::lazy::set_capture_enabled): while
+// set, elementwise ops on a device with a lazy backend are recorded and
+// realized on first read.
+void lref_set_capture(int on) { lmp::tensor::lazy::set_capture_enabled(on != 0); }
 
 }  // extern "C"

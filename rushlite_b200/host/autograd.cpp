@@ -183,6 +183,19 @@ void Variable::backward() {
   std::unordered_set<void*> seen;
   dfs(*this, seen, topo);
   std::reverse(topo.begin(), topo.end());
+  // A repeated backward over the same graph accumulates into every node's
+  // gradient, intermediates included, as the reference's eager sweep does.
+  // Intermediate gradients left pending by the previous sweep are read by
+  // other pending gradients of that sweep, so they are materialised before
+  // this sweep updates them in place.  A first sweep finds only untouched
+  // constant gradients (zeros; the seed is replaced, not updated) and skips this.
+  std::vector<ImplPtr> stale;
+  for (Variable& node : topo) {
+    if (!node.grad_fn() || !node.requires_grad() || !node.impl()->grad.defined()) continue;
+    const ImplPtr& gi = node.impl()->grad.impl();
+    if (gi->lazy && gi->lazy->kind != LazyNode::kConst) stale.push_back(gi);
+  }
+  if (!stale.empty()) tensor::realize_all(stale);
   impl_->grad = tensor::ones_like(impl_->grad);
   {
     tensor::lazy::CaptureGuard cap(true);
