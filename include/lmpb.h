@@ -234,6 +234,35 @@ lmpb_status lmpb_copy(int kind, const void* src, int src_dtype, void* dst, int d
  * (csrc/src/autograd/variable.cpp:30-35). */
 lmpb_status lmpb_add_inplace(int dtype, void* dst, const void* src, int64_t n, void* stream);
 
+/* ------------------------------------------------- multi-GPU collectives */
+
+/* The reference is single-device; these serve the exchange steps of the
+ * row-partitioned multi-GPU paths built on it (one process per GPU): the
+ * all-reduce of a leading-axis reduction's partials and of data-parallel
+ * gradients.  NCCL underneath, loaded at run time; LMPB_ERR_UNSUPPORTED when
+ * it is absent.  No counterpart in the reference. */
+#define LMPB_COMM_ID_BYTES 128
+
+/* Writes a new communicator id (LMPB_COMM_ID_BYTES bytes) for rank 0 to
+ * share with the other ranks (through the launcher's store, for example). */
+lmpb_status lmpb_comm_unique_id(void* id, size_t bytes);
+/* Joins this process, on the current CUDA device, to the communicator of
+ * `nranks` ranks named by `id`.  One communicator per process. */
+lmpb_status lmpb_comm_init(const void* id, int nranks, int rank);
+lmpb_status lmpb_comm_destroy(void);
+/* Number of ranks of the communicator (0 before lmpb_comm_init). */
+int lmpb_comm_size(void);
+/* In-place all-reduce (`op` an lmpb_reduce_op) of `nbufs` device buffers of
+ * `dtype` (int32, int64, float32, float64) in one grouped launch.  With
+ * overlap = 0 it runs on `stream`, after the work already queued there.  With
+ * overlap = 1 it runs on the library's communication stream, still after the
+ * work queued on `stream`, so later kernels on `stream` proceed meanwhile;
+ * lmpb_comm_join(stream) then makes `stream` wait for every overlapped
+ * all-reduce issued so far.  Both forms can be recorded by stream capture. */
+lmpb_status lmpb_allreduce(int dtype, void* const* bufs, const int64_t* counts, int nbufs, int op, int overlap,
+                           void* stream);
+lmpb_status lmpb_comm_join(void* stream);
+
 /* ------------------------------------------------------ fused kernels */
 
 /* The lazy-fusion compiler behind capture_on / capture.  Replaces the NVRTC

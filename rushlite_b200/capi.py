@@ -42,8 +42,10 @@ EXPORTS = [
     "lmpb_reduce", "lmpb_matmul", "lmpb_gemm_f32", "lmpb_transpose", "lmpb_malloc", "lmpb_free",
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
     "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error", "lmpb_reduce_noalloc",
-    "lmpb_gemm_f32_bias_act",
+    "lmpb_gemm_f32_bias_act", "lmpb_comm_unique_id", "lmpb_comm_init", "lmpb_comm_destroy", "lmpb_comm_size",
+    "lmpb_allreduce", "lmpb_comm_join",
 ]
+COMM_ID_BYTES = 128
 
 
 class LmpbError(RuntimeError):
@@ -100,6 +102,12 @@ def lib() -> C.CDLL:
         L.lmpb_fused_release.argtypes = [vp]
         L.lmpb_fused_source.argtypes = [vp]
         L.lmpb_fused_source.restype = C.c_char_p
+        L.lmpb_comm_unique_id.argtypes = [vp, C.c_size_t]
+        L.lmpb_comm_init.argtypes = [vp, i32, i32]
+        L.lmpb_comm_destroy.argtypes = []
+        L.lmpb_comm_size.argtypes = []
+        L.lmpb_allreduce.argtypes = [i32, C.POINTER(vp), P64, i32, i32, i32, vp]
+        L.lmpb_comm_join.argtypes = [vp]
         for name in EXPORTS:
             if name not in ("lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_fused_source"):
                 getattr(L, name).restype = C.c_int
@@ -214,3 +222,36 @@ def kernel_launches() -> int:
 def device_error() -> None:
     """Raises if a bounded device wait expired since the last call."""
     check(lib().lmpb_device_error())
+
+
+# ------------------------------------------------------------ collectives
+
+def comm_unique_id() -> bytes:
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    check(lib().lmpb_comm_unique_id(buf, COMM_ID_BYTES))
+    return buf.raw
+
+
+def comm_init(uid: bytes, nranks: int, rank: int) -> None:
+    buf = C.create_string_buffer(uid, COMM_ID_BYTES)
+    check(lib().lmpb_comm_init(buf, nranks, rank))
+
+
+def comm_destroy() -> None:
+    check(lib().lmpb_comm_destroy())
+
+
+def comm_size() -> int:
+    return int(lib().lmpb_comm_size())
+
+
+def allreduce(dtype, ptrs, counts, op=SUM, overlap=False, stream=0) -> None:
+    """In-place all-reduce of device buffers in one grouped launch (lmpb_allreduce)."""
+    n = len(ptrs)
+    pa = (C.c_void_p * max(1, n))(*ptrs)
+    ca = (C.c_int64 * max(1, n))(*counts)
+    check(lib().lmpb_allreduce(dtype, pa, ca, n, op, int(overlap), stream))
+
+
+def comm_join(stream=0) -> None:
+    check(lib().lmpb_comm_join(stream))

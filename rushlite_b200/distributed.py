@@ -42,6 +42,54 @@ def init(backend: str | None = None):
     return rank, world, local
 
 
+def init_comm() -> bool:
+    """Creates the library's own device communicator (lmpb_comm_init, NCCL)
+    for the torch.distributed job this process belongs to: rank 0 makes the id,
+    the process group broadcasts it.  Collectives through it run on the host
+    layer's stream, so they order after the kernels that feed them and can be
+    recorded into a CUDA graph with the step.  Returns False for one rank."""
+    import torch.distributed as dist
+
+    from . import capi
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return False
+    if capi.comm_size():
+        return True
+    box = [capi.comm_unique_id() if dist.get_rank() == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    capi.comm_init(box[0], dist.get_world_size(), dist.get_rank())
+    return True
+
+
+def _stream():
+    from . import _C
+
+    return _C.cuda.current_stream()
+
+
+def all_reduce_many(tensors, op: str = "sum", overlap: bool = False):
+    """In-place all-reduce of backend CUDA tensors of one dtype through the
+    library's communicator, as one grouped launch.  overlap=True runs it on
+    the communication stream (ordered after the work queued so far), so the
+    kernels that follow proceed; join() orders the host layer's stream after it."""
+    from . import capi
+
+    if not tensors:
+        return
+    dt = int(tensors[0].dtype.value)
+    ptrs = [t.data_ptr() for t in tensors]
+    counts = [int(np.prod(t.shape)) for t in tensors]
+    capi.allreduce(dt, ptrs, counts, capi.REDUCE_OPS[op], overlap, _stream())
+
+
+def join():
+    """Makes the host layer's stream wait for every overlapped all-reduce."""
+    from . import capi
+
+    capi.comm_join(_stream())
+
+
 def shard_rows(n: int, rank: int, world: int) -> tuple[int, int]:
     """Contiguous block of rows [r0, r1) owned by `rank`; blocks differ by at most one row."""
     base, extra = divmod(n, world)
@@ -50,13 +98,21 @@ def shard_rows(n: int, rank: int, world: int) -> tuple[int, int]:
 
 
 def all_reduce_(x, op: str = "sum"):
-    """In-place all-reduce of a backend tensor (rushlite_b200 _Tensor on CUDA,
-    zero-copy through __cuda_array_interface__) or of a NumPy array (gloo)."""
+    """In-place all-reduce of a backend tensor (rushlite_b200 _Tensor on CUDA)
+    or of a NumPy array (gloo).  A CUDA tensor goes through the library's
+    communicator when init_comm() created one, else through torch.distributed
+    (zero-copy via __cuda_array_interface__)."""
     import torch
     import torch.distributed as dist
 
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return x
+    if not isinstance(x, np.ndarray):
+        from . import capi
+
+        if capi.comm_size():
+            all_reduce_many([x], op)
+            return x
     rop = getattr(dist.ReduceOp, _OPS[op])
     if isinstance(x, np.ndarray):
         dist.all_reduce(torch.from_numpy(x), op=rop)

@@ -58,19 +58,23 @@ def _mlp_grads(rsl, params, x, y):
     return loss, P
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, mode="gloo"):
     try:
         sys.path.insert(0, ROOT)
+        dev = rank if mode == "lmpb" else 0
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
-                          WORLD_SIZE=str(world), LOCAL_RANK="0")
+                          WORLD_SIZE=str(world), LOCAL_RANK=str(dev))
         import torch
         import torch.distributed as dist
 
-        torch.cuda.set_device(0)
+        torch.cuda.set_device(dev)
         import rushlite_b200 as rsl
         from rushlite_b200 import distributed as D
 
+        rsl.cuda.set_device(dev)
         dist.init_process_group("gloo", rank=rank, world_size=world)
+        if mode == "lmpb":
+            assert D.init_comm()  # the library's NCCL communicator carries all_reduce_
         out = {}
         # --- C3, row-sharded
         R, Cn = 4096, 4096
@@ -107,6 +111,16 @@ def _worker(rank, world, port, q):
         out["dp_loss"] = (loss.numpy(), loss1.numpy())
         for i, (p, p1) in enumerate(zip(P, P1)):
             out[f"dp_grad{i}"] = (p.grad.numpy(), p1.grad.numpy())
+        if mode == "lmpb":
+            # overlapped all-reduce on the communication stream, then join
+            g = [p.grad for p in P1]
+            before = [x.numpy() for x in g]
+            D.all_reduce_many(g, "sum", overlap=True)
+            D.join()
+            out["overlap"] = [(x.numpy(), 2 * b) for x, b in zip(g, before)]
+            from rushlite_b200 import capi
+
+            capi.comm_destroy()
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, out, None))
@@ -114,13 +128,19 @@ def _worker(rank, world, port, q):
         q.put((rank, None, traceback.format_exc()))
 
 
-def test_two_ranks_on_product_kernels(cuda):
+@pytest.mark.parametrize("mode", ["gloo", "lmpb"])
+def test_two_ranks_on_product_kernels(cuda, mode):
+    """gloo: both ranks on GPU 0, all-reduce through torch's gloo group.
+    lmpb: one rank per GPU (needs two), all-reduce through the library's own
+    NCCL communicator (lmpb_allreduce), blocking and overlapped."""
     from tests.util import assert_bitexact, rel_err
 
+    if mode == "lmpb" and cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     results = {}
@@ -141,6 +161,8 @@ def test_two_ranks_on_product_kernels(cuda):
         assert rel_err(*out["sum_dim0"]) <= 1e-5
         assert_bitexact(*out["sum_dim1"], f"rank {rank} sum dim1")
         assert rel_err(*out["dp_loss"]) <= 1e-5
-        for k, (g, g1) in out.items():
-            if k.startswith("dp_grad"):
-                assert rel_err(g, g1) <= 1e-5, (rank, k, rel_err(g, g1))
+        for k in [k for k in out if k.startswith("dp_grad")]:
+            g, g1 = out[k]
+            assert rel_err(g, g1) <= 1e-5, (rank, k, rel_err(g, g1))
+        for got, want in out.get("overlap", []):
+            assert_bitexact(got, want, f"rank {rank} overlapped all-reduce")
