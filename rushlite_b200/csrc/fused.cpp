@@ -102,6 +102,7 @@ struct Plan {
   int64_t S = 1;                   // column-reduce row chunks
   bool warp_rows = false;          // row-reduce: warp per row
   int row_unroll = 1;              // row-reduce: unroll factor of the walk along a row
+  int stream = 0;                  // 1: full-size outputs use evict-first stores; 2: leaf loads too
 };
 
 }  // namespace
@@ -235,6 +236,7 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
     const int v = atoi(e);  // tuning override: 1, 2, 4, 8 or 16
     if (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) want = v;
   }
+  if (const char* e = getenv("LMPB_FUSED_STREAM")) p.stream = std::max(0, std::min(2, atoi(e)));  // tuning override
   p.vec = 1;
   for (int v = want; v > 1; v >>= 1)
     if (inner % v == 0) { p.vec = v; break; }
@@ -306,8 +308,12 @@ struct Gen {
       const std::string src = "L" + std::to_string(nd.a);
       const std::string LT = tname(h.leaves[nd.a].dtype);
       if (L) {
-        os << "    " << ind << "Pack<" << LT << ", " << vec << "> pk" << m << " = *reinterpret_cast<const Pack<" << LT
-           << ", " << vec << ">*>(" << src << " + " << leaf_off[nd.a] << ");\n";
+        if (p.stream >= 2 && (vec * (int)lmpb::dtype_size(h.leaves[nd.a].dtype)) % 16 == 0)
+          os << "    " << ind << "Pack<" << LT << ", " << vec << "> pk" << m << " = ld_cs<" << LT << ", " << vec << ">("
+             << src << " + " << leaf_off[nd.a] << ");\n";
+        else
+          os << "    " << ind << "Pack<" << LT << ", " << vec << "> pk" << m << " = *reinterpret_cast<const Pack<" << LT
+             << ", " << vec << ">*>(" << src << " + " << leaf_off[nd.a] << ");\n";
         os << decl << ";\n";
         os << "    " << ind << "#pragma unroll\n    " << ind << "for (int j = 0; j < " << vec << "; ++j) v" << m
            << "[j] = static_cast<" << T << ">(pk" << m << ".v[j]);\n";
@@ -341,16 +347,22 @@ struct Gen {
       const int m = h.outs[j].node;
       const std::string OT = tname(h.outs[j].dtype);
       const std::string O = "O" + std::to_string(j);
+      const bool cs = p.stream >= 1 && (vec * (int)lmpb::dtype_size(h.outs[j].dtype)) % 16 == 0;
       if (vec > 1) {
         os << "    " << ind << "{ Pack<" << OT << ", " << vec << "> po;\n";
-        if (mode == LMPB_OUT_ACCUM)
+        if (mode == LMPB_OUT_ACCUM && cs)
+          os << "    " << ind << "  po = ld_cs<" << OT << ", " << vec << ">(" << O << " + " << off << ");\n";
+        else if (mode == LMPB_OUT_ACCUM)
           os << "    " << ind << "  po = *reinterpret_cast<const Pack<" << OT << ", " << vec << ">*>(" << O << " + " << off << ");\n";
         os << "    " << ind << "  #pragma unroll\n    " << ind << "  for (int j = 0; j < " << vec << "; ++j) po.v[j] = ";
         if (mode == LMPB_OUT_ACCUM)
           os << "lmpb_dev::r_add<" << OT << ">(po.v[j], static_cast<" << OT << ">(" << ref(m, true) << "));\n";
         else
           os << "static_cast<" << OT << ">(" << ref(m, true) << ");\n";
-        os << "    " << ind << "  *reinterpret_cast<Pack<" << OT << ", " << vec << ">*>(" << O << " + " << off << ") = po; }\n";
+        if (cs)
+          os << "    " << ind << "  st_cs<" << OT << ", " << vec << ">(" << O << " + " << off << ", po); }\n";
+        else
+          os << "    " << ind << "  *reinterpret_cast<Pack<" << OT << ", " << vec << ">*>(" << O << " + " << off << ") = po; }\n";
       } else {
         if (mode == LMPB_OUT_ACCUM)
           os << "    " << ind << O << "[" << off << "] = lmpb_dev::r_add<" << OT << ">(" << O << "[" << off << "], static_cast<" << OT << ">(" << ref(m, false) << "));\n";
@@ -573,6 +585,13 @@ std::string generate(lmpb_fused_s& h) {
   std::ostringstream src;
   src << "// generated by lmpb fused compiler\n" << kOpsDeviceSource << "\n";
   src << "template <typename T, int V> struct alignas(sizeof(T) * V >= 16 ? 16 : sizeof(T) * V) Pack { T v[V]; };\n";
+  // evict-first (streaming) 16-byte accesses, for data touched once per pass
+  src << "template <typename T, int V> __device__ __forceinline__ void st_cs(T* p, const Pack<T, V>& v) {\n"
+         "  const uint4* s = reinterpret_cast<const uint4*>(&v); uint4* d = reinterpret_cast<uint4*>(p);\n"
+         "  #pragma unroll\n  for (int i = 0; i < (int)(sizeof(Pack<T, V>) / 16); ++i) __stcs(d + i, s[i]);\n}\n"
+         "template <typename T, int V> __device__ __forceinline__ Pack<T, V> ld_cs(const T* p) {\n"
+         "  Pack<T, V> v; uint4* d = reinterpret_cast<uint4*>(&v); const uint4* s = reinterpret_cast<const uint4*>(p);\n"
+         "  #pragma unroll\n  for (int i = 0; i < (int)(sizeof(Pack<T, V>) / 16); ++i) d[i] = __ldcs(s + i);\n  return v;\n}\n";
   src << "template <typename T> __device__ __forceinline__ T warp_sum(T v) {\n"
          "  #pragma unroll\n  for (int d = 16; d > 0; d >>= 1) v = lmpb_dev::r_add<T>(v, static_cast<T>(__shfl_down_sync(0xffffffffu, v, d)));\n"
          "  return v;\n}\n";

@@ -6,13 +6,20 @@
 //  * inner  > 1 (leading / middle axis): a thread owns a 16-byte vector of
 //    adjacent columns and walks down the R rows, so every warp load is a
 //    fully coalesced 512-byte segment.  When outer x column-blocks cannot fill
-//    the 148 SMs, R is split into S chunks whose partials go to a workspace
-//    and a second kernel combines them in chunk order.  No float atomics, so
-//    results are identical run to run.
+//    the 148 SMs, R is split into chunks.  With enough column blocks, the 8
+//    chunks of a column block are one thread-block cluster: each CTA leaves
+//    its partial in shared memory and the cluster's first CTA folds the 8
+//    partials in chunk order through distributed shared memory, in the same
+//    kernel.  Otherwise the S chunks' partials go to a workspace and a second
+//    kernel combines them in chunk order.  No float atomics, so results are
+//    identical run to run.
 // Accumulation stays in the input dtype (the reference's functors are
 // instantiated on the output type, csrc/src/tensor/cpu/reduct.cpp:33-49),
 // which keeps int32 sums, max and min bit-exact with the reference; a float
 // sum differs from the reference's sequential order only by rounding.
+#include <cooperative_groups.h>
+
+#include <cstdlib>
 #include <limits>
 
 #include "common.cuh"
@@ -148,12 +155,11 @@ __global__ void __launch_bounds__(kThreads)
 // partials are folded in lane order through shared memory and the CTA's
 // partial goes to dst[(chunk * outer + o) * inner + c].  Narrow CTAs (CTX*VW
 // columns) fill the GPU with few row chunks, so the combine pass is small.
-constexpr int CTX = 16, CTY = kThreads / CTX;
-
-template <int OP, typename T, int VW>
+template <int OP, typename T, int VW, int CTX>
 __global__ void __launch_bounds__(kThreads)
     reduce_cols_kernel(const T* __restrict__ in, T* __restrict__ dst, int64_t outer, int64_t R, int64_t inner,
                        int64_t rows_per_chunk) {
+  constexpr int CTY = kThreads / CTX;
   using Rd = RedOp<OP, T>;
   __shared__ T part[CTY][CTX * VW];
   const int tx = threadIdx.x % CTX, ty = threadIdx.x / CTX;
@@ -201,6 +207,80 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// The column kernel for a cluster of kClusterChunks CTAs along the chunk
+// axis: the CTAs walk their row chunks as reduce_cols_kernel does, fold their
+// row lanes into `fin` in shared memory, and the cluster's rank-0 CTA folds
+// the ranks' `fin` in rank (= chunk) order through distributed shared memory
+// and writes the output: no workspace and no second launch.
+constexpr int kClusterChunks = 8;
+
+// Chunks per cluster: 8 (portable) or 16 (LMPB_REDUCE_CLUSTER=16, a
+// non-portable cluster size B200 supports).
+int cluster_chunks() {
+  const char* e = getenv("LMPB_REDUCE_CLUSTER");
+  return (e && atoi(e) == 16) ? 16 : kClusterChunks;
+}
+
+template <int OP, typename T, int VW, int CC>
+__global__ void __launch_bounds__(kThreads)
+    reduce_cols_cluster_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t R, int64_t inner,
+                               int64_t rows_per_chunk) {
+  namespace cg = cooperative_groups;
+  constexpr int CTX = 16, CTY = kThreads / CTX;
+  using Rd = RedOp<OP, T>;
+  __shared__ T part[CTY][CTX * VW];
+  __shared__ T fin[CTX * VW];
+  const int tx = threadIdx.x % CTX, ty = threadIdx.x / CTX;
+  const int64_t c = ((int64_t)blockIdx.x * CTX + tx) * VW;
+  const int64_t o = blockIdx.y;
+  const int64_t r0 = (int64_t)blockIdx.z * rows_per_chunk;
+  const int64_t r1 = min(R, r0 + rows_per_chunk);
+  T acc[VW];
+#pragma unroll
+  for (int j = 0; j < VW; ++j) acc[j] = Rd::identity();
+  if (c < inner) {
+    const T* base = in + (o * R) * inner + c;
+    int64_t r = r0 + ty;
+    for (; r + 3 * CTY < r1; r += 4 * CTY) {
+      V16<T> x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u * CTY) * inner));
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
+    }
+    for (; r < r1; r += CTY) {
+      V16<T> x;
+      x.raw = __ldg(reinterpret_cast<const uint4*>(base + r * inner));
+#pragma unroll
+      for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x.v[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VW; ++j) part[ty][tx * VW + j] = acc[j];
+  __syncthreads();
+  if (ty == 0) {
+#pragma unroll
+    for (int j = 0; j < VW; ++j) {
+      T v = part[0][tx * VW + j];
+      for (int k = 1; k < CTY; ++k) v = Rd::apply(v, part[k][tx * VW + j]);
+      fin[tx * VW + j] = v;
+    }
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();  // every rank's fin is written
+  if (cl.block_rank() == 0 && ty == 0 && c < inner) {
+#pragma unroll
+    for (int j = 0; j < VW; ++j) {
+      T v = fin[tx * VW + j];
+      for (int k = 1; k < CC; ++k) v = Rd::apply(v, cl.map_shared_rank(fin, k)[tx * VW + j]);
+      out[o * inner + c + j] = v;
+    }
+  }
+  cl.sync();  // the other ranks keep their shared memory until rank 0 has read it
+}
+
 // Combines S chunk partials: out[i] = op over s of part[s][i], in chunk order.
 // A CTA owns 32 adjacent columns (lane = column, coalesced); its 8 warps take
 // 8 contiguous runs of chunks, each with 8 independent loads in flight, and
@@ -245,13 +325,32 @@ __global__ void fill_identity_kernel(T* out, int64_t n) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Column threads per CTA of the column kernel: wider CTAs read longer
+// contiguous runs of each row (CTX * 16 bytes), narrower ones leave more
+// CTAs to spread over the SMs when the tensor has few columns.
+int pick_ctx(int64_t inner, int vw) {
+  int ctx = 16;
+  if (const char* e = getenv("LMPB_REDUCE_CTX")) {  // tuning override: 16, 32, 64 or 128
+    const int v = atoi(e);
+    if (v == 16 || v == 32 || v == 64 || v == 128) return v;
+  }
+  (void)inner;
+  (void)vw;
+  return ctx;
+}
+
 template <typename T>
-int64_t pick_chunks(int64_t outer, int64_t R, int64_t inner, int vw) {
-  const int64_t colblocks = (inner / vw + CTX - 1) / CTX;
+int64_t pick_chunks(int64_t outer, int64_t R, int64_t inner, int vw, int ctx) {
+  const int64_t colblocks = (inner / vw + ctx - 1) / ctx;
   const int64_t ctas = colblocks * outer;
+  // one wave: at most 8 resident CTAs per SM (256 threads, 4 KB shared
+  // memory each), so a chunk count that overshoots the slots leaves a second,
+  // nearly empty wave (measured: 1216 CTAs for 1184 slots cost ~15 %)
   const int64_t target = (int64_t)sm_count() * 8;
   if (ctas >= target || R < 64) return 1;
-  int64_t S = (target + ctas - 1) / ctas;
+  int64_t S = target / ctas;
+  if (const char* e = getenv("LMPB_REDUCE_CEIL"))  // A/B switch: the previous rounding up
+    if (atoi(e)) S = (target + ctas - 1) / ctas;
   if (S > R / 16) S = R / 16;  // keep >= 16 rows per chunk
   if (S < 1) S = 1;
   return S;
@@ -264,17 +363,30 @@ struct ReducePlan {
   int64_t outer, R, inner;
   int64_t S;  // chunks (1 = no workspace)
   int vw;     // column vector width
+  int ctx;    // column threads per CTA
+  bool cluster;  // the chunks are one thread-block cluster (S = kClusterChunks, no workspace)
   size_t ws_bytes;
 };
 
 template <typename T>
 static ReducePlan plan_reduce(const void* in, const void* out, int64_t outer, int64_t R, int64_t inner) {
-  ReducePlan p{outer, R, inner, 1, 1, 0};
+  ReducePlan p{outer, R, inner, 1, 1, 16, false, 0};
   if (inner > 1) {
     constexpr int N = V16<T>::N;
     p.vw = (inner % N == 0 && aligned16(in) && aligned16(out)) ? N : 1;
-    p.S = pick_chunks<T>(outer, R, inner, p.vw);
-    if (p.S > 1) p.ws_bytes = (size_t)p.S * outer * inner * sizeof(T);
+    p.ctx = pick_ctx(inner, p.vw);
+    p.S = pick_chunks<T>(outer, R, inner, p.vw, p.ctx);
+    // enough column blocks for two cluster CTAs per SM: fold the chunks in
+    // the cluster instead of through a workspace and a second kernel
+    const int64_t colblocks = (inner / p.vw + 15) / 16;
+    const char* e = getenv("LMPB_REDUCE_CLUSTER");  // A/B switch: 0 keeps the workspace path
+    const int cc = cluster_chunks();
+    if (p.S > 1 && p.vw == N && p.ctx == 16 && outer <= 65535 && R >= 16 * cc &&
+        colblocks * outer * cc >= (int64_t)sm_count() * 2 && !(e && atoi(e) == 0)) {
+      p.cluster = true;
+      p.S = cc;
+    }
+    if (p.S > 1 && !p.cluster) p.ws_bytes = (size_t)p.S * outer * inner * sizeof(T);
   }
   return p;
 }
@@ -302,16 +414,56 @@ static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, c
     return launch_status("reduce_rows_kernel");
   }
   constexpr int N = V16<T>::N;
-  const int64_t colblocks = (p.inner / p.vw + CTX - 1) / CTX;
+  const int64_t colblocks = (p.inner / p.vw + p.ctx - 1) / p.ctx;
   const int64_t rows_per_chunk = (p.R + p.S - 1) / p.S;
   if (p.outer > 65535 || p.S > 65535)
     return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce: outer extent too large for the column kernel");
   dim3 grid((unsigned)colblocks, (unsigned)p.outer, (unsigned)p.S);
+  if (p.cluster) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = (unsigned)p.S;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (p.S == 16) {
+      auto k = reduce_cols_cluster_kernel<OP, T, N, 16>;
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, k, in, out, p.R, p.inner, rows_per_chunk);
+    } else {
+      e = cudaLaunchKernelEx(&cfg, reduce_cols_cluster_kernel<OP, T, N, kClusterChunks>, in, out, p.R, p.inner,
+                             rows_per_chunk);
+    }
+    if (e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("reduce_cols_cluster_kernel: ") + cudaGetErrorString(e));
+    return launch_status("reduce_cols_cluster_kernel");
+  }
   T* dst = p.S > 1 ? ws : out;
-  if (p.vw == N)
-    reduce_cols_kernel<OP, T, N><<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
-  else
-    reduce_cols_kernel<OP, T, 1><<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
+  auto launch = [&](auto vw_c, auto ctx_c) {
+    reduce_cols_kernel<OP, T, decltype(vw_c)::value, decltype(ctx_c)::value>
+        <<<grid, kThreads, 0, st>>>(in, dst, p.outer, p.R, p.inner, rows_per_chunk);
+  };
+  using I16 = std::integral_constant<int, 16>;
+  using I32 = std::integral_constant<int, 32>;
+  using I64 = std::integral_constant<int, 64>;
+  using I128 = std::integral_constant<int, 128>;
+  using VN = std::integral_constant<int, N>;
+  using V1 = std::integral_constant<int, 1>;
+  if (p.vw == N) {
+    switch (p.ctx) {
+      case 32: launch(VN{}, I32{}); break;
+      case 64: launch(VN{}, I64{}); break;
+      case 128: launch(VN{}, I128{}); break;
+      default: launch(VN{}, I16{}); break;
+    }
+  } else {
+    launch(V1{}, I16{});
+  }
   lmpb_status s = launch_status("reduce_cols_kernel");
   if (s != LMPB_OK || p.S == 1) return s;
   const int64_t g2 = (nout + 31) / 32;

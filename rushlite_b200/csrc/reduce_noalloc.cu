@@ -27,8 +27,10 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
 namespace {
 
 // The split plan targets 8 CTAs per SM, each CTA 16 column threads of 16
-// bytes, so its workspace is at most about 8 x SMs x 256 B (0.3 MB on a
-// 148-SM B200); 1 MiB covers it with margin.
+// bytes, so its workspace is at most 8 x SMs x 256 B (0.3 MB on a 148-SM
+// B200); 1 MiB covers it with margin.  The size check in
+// lmpb_reduce_noalloc therefore cannot fail on a B200: it would take a GPU
+// with more than 512 SMs.
 constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
 
 // The scratch itself.  Host code must not pass `g_noalloc_scratch` to a

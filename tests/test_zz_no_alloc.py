@@ -23,9 +23,13 @@ def _noalloc(op, dt, in_ptr, shape, axis, out_ptr):
                                               out_ptr, None))
 
 
-# [16384, 4096] axis 0 uses the split-row workspace (the C3 column case)
-CASES = [((16384, 4096), 0, np.float32), ((16384, 4096), 0, np.int32), ((4096, 3000), 0, np.float32),
-         ((2048, 1024), 1, np.float32)]
+# Narrow leading-axis reductions split their rows over many chunks whose
+# partials live in the scratch array ([65536, 256] axis 0: 296 chunks, 0.3 MB;
+# [100000, 100] axis 0: 592 chunks).  The C3 column case [16384, 4096] axis 0
+# folds its chunks inside a thread-block cluster and needs no scratch at all;
+# the last axis never does.
+CASES = [((65536, 256), 0, np.float32), ((65536, 256), 0, np.int32), ((100000, 100), 0, np.float32),
+         ((16384, 4096), 0, np.float32), ((2048, 1024), 1, np.float32)]
 
 
 @pytest.mark.parametrize("shape,axis,dt", CASES)
