@@ -201,6 +201,17 @@ lmpb_status lmpb_gemm_f32_bias_act(int trans_a, int trans_b, const float* A, con
                                    int64_t m, int64_t n, int64_t k, const float* bias, int clamp,
                                    double lo, double hi, void* stream);
 
+/* The tensor-core GEMM's work schedule, the same functions its kernels run,
+ * exported so that tests can check it without a GPU.  Output tile t (tiles
+ * of tm x tn, tile rows grouped by 8) starts at (*m0, *n0); split-K unit u
+ * covers tile *t over k-blocks [*kb0, *kb1); lmpb_gemm_sched_splits returns
+ * the split count for ntiles tiles of num_kb k-blocks on `clusters` CTA pairs
+ * (forced > 0: a requested count, reduced until no unit is empty).  No
+ * counterpart in the reference. */
+void lmpb_gemm_sched_tile(int t, int tiles_m, int tiles_n, int tm, int tn, int* m0, int* n0);
+void lmpb_gemm_sched_unit(int u, int splits, int num_kb, int* t, int* kb0, int* kb1);
+int lmpb_gemm_sched_splits(int64_t ntiles, int num_kb, int clusters, int forced);
+
 /* LMPB_ERR_TIMEOUT if a bounded device wait inside a kernel expired since
  * the last call (the kernel then stopped early and its output is invalid),
  * else LMPB_OK.  Synchronises the current device.  No counterpart in the

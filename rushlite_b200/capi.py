@@ -43,7 +43,7 @@ EXPORTS = [
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
     "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error", "lmpb_reduce_noalloc",
     "lmpb_gemm_f32_bias_act", "lmpb_comm_unique_id", "lmpb_comm_init", "lmpb_comm_destroy", "lmpb_comm_size",
-    "lmpb_allreduce", "lmpb_comm_join",
+    "lmpb_allreduce", "lmpb_comm_join", "lmpb_gemm_sched_tile", "lmpb_gemm_sched_unit", "lmpb_gemm_sched_splits",
 ]
 COMM_ID_BYTES = 128
 
@@ -108,7 +108,15 @@ def lib() -> C.CDLL:
         L.lmpb_comm_size.argtypes = []
         L.lmpb_allreduce.argtypes = [i32, C.POINTER(vp), P64, i32, i32, i32, vp]
         L.lmpb_comm_join.argtypes = [vp]
+        PI = C.POINTER(C.c_int)
+        L.lmpb_gemm_sched_tile.argtypes = [i32, i32, i32, i32, i32, PI, PI]
+        L.lmpb_gemm_sched_tile.restype = None
+        L.lmpb_gemm_sched_unit.argtypes = [i32, i32, i32, PI, PI, PI]
+        L.lmpb_gemm_sched_unit.restype = None
+        L.lmpb_gemm_sched_splits.argtypes = [i64, i32, i32, i32]
         for name in EXPORTS:
+            if name in ("lmpb_gemm_sched_tile", "lmpb_gemm_sched_unit"):
+                continue
             if name not in ("lmpb_last_error", "lmpb_version", "lmpb_kernel_launches", "lmpb_fused_source"):
                 getattr(L, name).restype = C.c_int
         _lib = L

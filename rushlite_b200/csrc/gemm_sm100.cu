@@ -402,25 +402,60 @@ __global__ void __launch_bounds__(256)
 
 // Tile t of a tiles_m x tiles_n grid in grouped order: 8 row-tiles at a time
 // walk the column tiles, so concurrently running CTAs share B panels in L2.
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m0, int& n0) {
+// Work schedule, shared by the kernels and the host (and exported below so
+// that tests check the very code the kernels run).
+//
+// Output tiles are visited in groups of 8 tile rows: tile t of a group walks
+// down the group's rows first, so consecutive tiles share B columns in L2.
+__host__ __device__ __forceinline__ void sched_tile(int t, int tiles_m, int tiles_n, int tm, int tn, int& m0,
+                                                    int& n0) {
   const int group = 8;
   const int g = t / (group * tiles_n);
   const int first_m = g * group;
   const int gsize = min(tiles_m - first_m, group);
   const int local = t % (group * tiles_n);
-  m0 = (first_m + local % gsize) * BM;
-  n0 = (local / gsize) * BN;
+  m0 = (first_m + local % gsize) * tm;
+  n0 = (local / gsize) * tn;
+}
+
+// Split-K units: unit u is tile u / splits over k-blocks [kb0, kb1) of
+// split u % splits, each split ceil(num_kb / splits) k-blocks long.
+__host__ __device__ __forceinline__ void sched_unit(int u, int splits, int num_kb, int& t, int& kb0, int& kb1) {
+  const int kb_per = (num_kb + splits - 1) / splits;
+  t = u / splits;
+  kb0 = (u % splits) * kb_per;
+  kb1 = min(num_kb, kb0 + kb_per);
+}
+
+// A requested split count, reduced until every unit has a k-block: the last
+// unit starts at (splits - 1) * kb_per, which must be below num_kb.
+__host__ __device__ __forceinline__ int sched_clamp_splits(int splits, int num_kb) {
+  splits = max(1, min(splits, max(1, num_kb)));
+  while (splits > 1 && (splits - 1) * ((num_kb + splits - 1) / splits) >= num_kb) --splits;
+  return splits;
+}
+
+// The split count the pair kernel runs with: forced > 0 is a tuning override
+// (clamped as above); otherwise K is split in two when the run gets >= 5 %
+// shorter, time ~ rounds(units) / splits with rounds = ceil(units / clusters),
+// and only for long K (>= 256 k-blocks, K >= 8192): measured on B200, a split
+// unit costs more than its share of the MMAs (4096^3: 2 splits 0.50 ms vs
+// 0.46 ms unsplit, 4 splits 1.1 ms; 4096 x 8192 x 4096: 0.80 vs 0.84 ms;
+// K = 32768: 2.8 vs 3.35 ms).
+inline int sched_choose_splits(int64_t ntiles, int num_kb, int clusters, int forced) {
+  if (clusters <= 0) return 1;
+  if (forced > 0) return sched_clamp_splits(forced, num_kb);
+  auto cost = [&](int sp) { return (double)((ntiles * sp + clusters - 1) / clusters) / sp; };
+  return (num_kb >= 256 && cost(2) < cost(1) * 0.95) ? 2 : 1;
+}
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m0, int& n0) {
+  sched_tile(t, tiles_m, tiles_n, BM, BN, m0, n0);
 }
 
 // As tile_coords, for the pair kernel's 256-row tiles.
 __device__ __forceinline__ void tile_coords_pair(int t, int tiles_m, int tiles_n, int& m0, int& n0) {
-  const int group = 8;
-  const int g = t / (group * tiles_n);
-  const int first_m = g * group;
-  const int gsize = min(tiles_m - first_m, group);
-  const int local = t % (group * tiles_n);
-  m0 = (first_m + local % gsize) * P_TM;
-  n0 = (local / gsize) * BN;
+  sched_tile(t, tiles_m, tiles_n, P_TM, BN, m0, n0);
 }
 
 // Optional epilogue after the product: + bias[col] (a row of n, fp32) then
@@ -744,7 +779,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   // ks = u % splits; with splits > 1 the unit that finishes a tile last sums
   // the partials (see the epilogue).
   const int num_units = tiles_m * tiles_n * splits;
-  const int kb_per = (num_kb + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P_STAGES; ++s) {
@@ -775,8 +809,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int u = pair; u < num_units && ok; u += npairs) {
-      const int t = u / splits, kb0 = (u % splits) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-      int m0, n0;
+      int t, kb0, kb1, m0, n0;
+      sched_unit(u, splits, num_kb, t, kb0, kb1);
       tile_coords_pair(t, tiles_m, tiles_n, m0, n0);
       const int ya = m0 + (int)rank * 128, yb = n0 + (int)rank * 128;
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -803,7 +837,8 @@ __global__ void __launch_bounds__(kThreadsP, 1)
     bool ok = true;
     int lt = 0;
     for (int u = pair; u < num_units && ok; u += npairs, ++lt) {
-      const int kb0 = (u % splits) * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+      int t_unused, kb0, kb1;
+      sched_unit(u, splits, num_kb, t_unused, kb0, kb1);
       if (!mbar_wait(smem_u32(&tempty[0]), (lt & 1) ^ 1, 6)) break;  // both epilogues drained
       tc_fence_after();
       const uint32_t dbig = tmem, dsmall = tmem + (uint32_t)BN;
@@ -1094,23 +1129,8 @@ lmpb_status gemm_f32_sm100(int trans_a, int trans_b, const float* A, const float
   const int nkb = (int)(Kp / BK), bflag = beta != 0.f ? 1 : 0;
   if (s == LMPB_OK && pair) {
     int clusters = pair_clusters();
-    // Split K in two when it shortens the run: time ~ rounds(units) / splits
-    // with rounds = ceil(ntiles * splits / clusters), a gain of 5 % required.
-    // Measured on B200, a split unit costs more than its share of the MMAs
-    // (4096^3: 2 splits 0.50 ms vs 0.46 ms unsplit, 4 splits 1.1 ms), so
-    // only long K (>= 256 k-blocks, K >= 8192) is split, and only in two
-    // (4096 x 8192 x 4096: 0.80 ms vs 0.84 ms; K = 32768: 2.8 ms vs 3.35 ms).
     const char* force = getenv("LMPB_GEMM_SPLITK");  // tuning override: the split count (1 = none)
-    if (clusters > 0 && force) {
-      splits = std::max(1, std::min(atoi(force), std::max(1, nkb)));
-      // every unit needs at least one k-block: with kb_per = ceil(nkb / splits)
-      // the last unit starts at (splits - 1) * kb_per, which must be < nkb
-      while (splits > 1 && (splits - 1) * ((nkb + splits - 1) / splits) >= nkb) --splits;
-    } else if (clusters > 0) {
-      auto cost = [&](int sp) { return (double)((ntiles * sp + clusters - 1) / clusters) / sp; };
-      double best = cost(1);
-      if (nkb >= 256 && cost(2) < best * 0.95) splits = 2;
-    }
+    splits = sched_choose_splits(ntiles, nkb, clusters, force ? std::max(1, atoi(force)) : 0);
     void* sk = nullptr;
     float* part = nullptr;
     unsigned* arrivals = nullptr;
@@ -1168,3 +1188,14 @@ unsigned int gemm_take_error() {
 }
 
 }  // namespace lmpb
+
+// The schedule helpers above, for tests (no counterpart in the reference).
+extern "C" void lmpb_gemm_sched_tile(int t, int tiles_m, int tiles_n, int tm, int tn, int* m0, int* n0) {
+  lmpb::sched_tile(t, tiles_m, tiles_n, tm, tn, *m0, *n0);
+}
+extern "C" void lmpb_gemm_sched_unit(int u, int splits, int num_kb, int* t, int* kb0, int* kb1) {
+  lmpb::sched_unit(u, splits, num_kb, *t, *kb0, *kb1);
+}
+extern "C" int lmpb_gemm_sched_splits(int64_t ntiles, int num_kb, int clusters, int forced) {
+  return lmpb::sched_choose_splits(ntiles, num_kb, clusters, forced);
+}

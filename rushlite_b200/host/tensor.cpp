@@ -272,13 +272,18 @@ Tensor Tensor::to(DeviceType device) const {
 // True when realizing `t` straight into storage `dst` (of shape `shape`) is
 // safe: every read of dst in the expression is at the index being written
 // (same shape, no broadcast) and dst carries no pending value of its own.
+// Below a matmul or a reduction the operands are read at other indices than
+// the one written, so dst must not appear there at all.
 static bool in_place_safe(const TensorImpl* t, const StorageImpl* dst, const std::vector<size_t>& shape,
-                          std::unordered_set<const TensorImpl*>& seen) {
-  if (!seen.insert(t).second) return true;
-  if (t->storage.get() == dst) return !t->lazy && t->shape == shape;
+                          std::unordered_set<const TensorImpl*>& seen, bool elementwise = true) {
+  // a node is checked once per context (elementwise or below a matmul/reduction)
+  const auto key = reinterpret_cast<const TensorImpl*>(reinterpret_cast<uintptr_t>(t) | (elementwise ? 0u : 1u));
+  if (!seen.insert(key).second) return true;
+  if (t->storage.get() == dst) return elementwise && !t->lazy && t->shape == shape;
   if (!t->lazy) return true;
+  const bool ew = elementwise && t->lazy->kind != LazyNode::kMatmul && t->lazy->kind != LazyNode::kReduceSum;
   for (const auto& in : t->lazy->inputs)
-    if (!in_place_safe(in.get(), dst, shape, seen)) return false;
+    if (!in_place_safe(in.get(), dst, shape, seen, ew)) return false;
   return true;
 }
 

@@ -110,3 +110,21 @@ def test_pending_matmul_realizes_when_read(rsl):
     eager = rsl.matmul(x, W).numpy()
     assert_bitexact(mv, eager, "pending product")
     assert_bitexact(yv, np.maximum(mv + bs, 0.0).astype(np.float32), "fused layer")
+
+
+def test_copy_of_linear_into_its_own_input(rsl):
+    """h.copy(relu(h @ W + b)): the pending value reads h through a matmul, at
+    other indices than the one written, so it must not be realized straight
+    into h's storage; the result equals the out-of-place layer."""
+    rng = np.random.default_rng(8)
+    hs = rng.standard_normal((256, 256)).astype(np.float32)
+    Ws = (rng.standard_normal((256, 256)) / 16).astype(np.float32)
+    bs = rng.standard_normal((256,)).astype(np.float32)
+    W, b = rsl.Variable(Ws), rsl.Variable(bs)
+    want = rsl.clamp(rsl.matmul(rsl.Variable(hs), W) + b, 0.0, FMAX).numpy()
+    h = rsl.Variable(hs)
+    p0 = h.data.data_ptr()
+    with rsl.no_grad(), rsl.capture_on():
+        h.data.copy(rsl.clamp(rsl.matmul(h, W) + b, 0.0, FMAX).data)
+    assert h.data.data_ptr() == p0
+    assert_bitexact(h.numpy(), want, "in-place copy of a Linear of its own input")

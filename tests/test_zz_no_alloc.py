@@ -32,6 +32,48 @@ CASES = [((65536, 256), 0, np.float32), ((65536, 256), 0, np.int32), ((100000, 1
          ((16384, 4096), 0, np.float32), ((2048, 1024), 1, np.float32)]
 
 
+def _pool_used():
+    """(current, high-water) bytes in use of the current device's default
+    stream-ordered pool, the pool lmpb_reduce takes its workspace from."""
+    rt = C.CDLL("libcudart.so.12")
+    dev, pool = C.c_int(), C.c_void_p()
+    assert rt.cudaGetDevice(C.byref(dev)) == 0
+    assert rt.cudaDeviceGetDefaultMemPool(C.byref(pool), dev) == 0
+    cur, high = C.c_uint64(), C.c_uint64()
+    # cudaMemPoolAttrUsedMemCurrent = 7, cudaMemPoolAttrUsedMemHigh = 8
+    assert rt.cudaMemPoolGetAttribute(pool, 7, C.byref(cur)) == 0
+    assert rt.cudaMemPoolGetAttribute(pool, 8, C.byref(high)) == 0
+    return cur.value, high.value, rt, pool
+
+
+def _reset_high(rt, pool):
+    zero = C.c_uint64(0)  # resets the high-water mark to the current use
+    assert rt.cudaMemPoolSetAttribute(pool, 8, C.byref(zero)) == 0
+
+
+def test_noalloc_allocates_nothing(cuda):
+    """The property the entry point exists for: its calls leave the device's
+    pool untouched, where lmpb_reduce on the same shape draws its workspace
+    from it (the control shows the check can see an allocation)."""
+    torch = cuda
+    shape = (65536, 256)
+    x = torch.randn(shape, device="cuda")
+    out = torch.empty((1, 256), device="cuda")
+    _noalloc(capi.SUM, capi.FLOAT32, x.data_ptr(), shape, 0, out.data_ptr())  # first call: symbol lookup
+    torch.cuda.synchronize()
+    cur, _, rt, pool = _pool_used()
+    _reset_high(rt, pool)
+    for _ in range(2):
+        _noalloc(capi.SUM, capi.FLOAT32, x.data_ptr(), shape, 0, out.data_ptr())
+    torch.cuda.synchronize()
+    cur2, high, _, _ = _pool_used()
+    assert high == cur and cur2 == cur, (cur, cur2, high)
+    capi.reduce(capi.SUM, capi.FLOAT32, x.data_ptr(), shape, 0, out.data_ptr())
+    torch.cuda.synchronize()
+    _, high2, _, _ = _pool_used()
+    assert high2 > cur, "the control allocation did not show in the pool's high-water mark"
+
+
 @pytest.mark.parametrize("shape,axis,dt", CASES)
 def test_noalloc_matches_lmpb_reduce_twice(cuda, shape, axis, dt):
     torch = cuda
