@@ -296,7 +296,12 @@ typedef enum {
   LMPB_FN_LEAF = 0,   /* reads leaf slot `a` */
   LMPB_FN_CONST = 1,  /* the constant p0 */
   LMPB_FN_BINARY = 2, /* binary op `sub` on nodes a, b (params p0/p1 for clamp_backward) */
-  LMPB_FN_UNARY = 3   /* unary op `sub` on node a (p0/p1 for clamp) */
+  LMPB_FN_UNARY = 3,  /* unary op `sub` on node a (p0/p1 for clamp) */
+  LMPB_FN_ROWRED = 4  /* LMPB_SUM or LMPB_MAX (`sub`) of node a over the last
+                         iteration dim; the same value along that dim.  The
+                         max and sum of a row softmax (layers/activation.py:26-40
+                         of the reference's Python layer) fuse with what reads
+                         them; equal bit for bit to the separate reduction */
 } lmpb_fnode_kind;
 
 typedef struct {

@@ -173,6 +173,11 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
     }
     p.out_mode[j] = mode;
   }
+  // in-kernel row reductions reduce the last iteration dim: keep it a group of its own
+  bool any_rowred = false;
+  for (const auto& n : h.nodes) any_rowred |= n.kind == LMPB_FN_ROWRED;
+  if (any_rowred && (nd == 0 || iter[nd - 1] <= 1))
+    return set_error(LMPB_ERR_INVALID, "fused: a row reduction needs a last iteration dim longer than 1");
   // collapse
   p.n = 1;
   for (int d = 0; d < nd; ++d) p.n *= iter[d];
@@ -183,6 +188,7 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
     std::vector<char> s;
     for (int i = 0; i < NL; ++i) s.push_back(lb[i][d]);
     for (int j = 0; j < NO; ++j) s.push_back(ob[j][d]);
+    s.push_back(any_rowred && d == nd - 1);
     if (G > 0 && gsig[G - 1] == s) {
       p.size[G - 1] *= iter[d];
       for (int i = 0; i < NL; ++i) p.leaf_stride[i][G - 1] = lstride[i][d];
@@ -208,7 +214,24 @@ lmpb_status make_plan(lmpb_fused_s& h, const int64_t* iter, int nd) {
   p.G = G;
   p.idx32 = p.n < (1ll << 31);
   // pattern
-  if (any_reduce) {
+  if (any_rowred) {
+    // one warp or CTA per row (the last dim); reduce outputs may only reduce the row
+    if (G == 1) {  // the whole space is one row
+      p.G = 2;
+      p.size[1] = p.size[0];
+      p.size[0] = 1;
+      for (auto& s : p.leaf_stride) { s[1] = s[0]; s[0] = 0; }
+      for (auto& s : p.out_stride) { s[1] = s[0]; s[0] = 0; }
+    } else if (G != 2) {
+      return set_error(LMPB_ERR_UNSUPPORTED, "fused: row reductions over a space of more than two groups");
+    }
+    for (int j = 0; j < NO; ++j) {
+      if (p.out_mode[j] < LMPB_OUT_REDUCE_SUM) continue;
+      if (p.out_stride[j][0] == 0 && p.size[0] > 1)
+        return set_error(LMPB_ERR_UNSUPPORTED, "fused: row reductions with a reduction over rows");
+    }
+    p.pattern = kRowReduce;
+  } else if (any_reduce) {
     std::vector<char> red;
     for (int j = 0; j < NO; ++j) {
       if (p.out_mode[j] != LMPB_OUT_REDUCE_SUM && p.out_mode[j] != LMPB_OUT_REDUCE_SUM_ACCUM) continue;
@@ -282,6 +305,7 @@ struct Gen {
         if (nd.kind == LMPB_FN_LEAF) v = p.leaf_stride[nd.a][g] != 0;
         else if (nd.kind == LMPB_FN_BINARY) v = varies[nd.a][g] || varies[nd.b][g];
         else if (nd.kind == LMPB_FN_UNARY) v = varies[nd.a][g];
+        else if (nd.kind == LMPB_FN_ROWRED) v = g < p.G - 1 && varies[nd.a][g];  // constant along its row
         varies[m][g] = v;
       }
     }
@@ -297,6 +321,7 @@ struct Gen {
   // Emits the computation of node m; `off` maps a leaf slot to its offset expression.
   void emit_node(int m, const std::string& ind, const std::vector<std::string>& leaf_off) {
     const lmpb_fnode& nd = h.nodes[m];
+    if (nd.kind == LMPB_FN_ROWRED) return;  // declared by its walk in gen_row_reduce
     const std::string T = tname(nd.dtype);
     const bool L = lane(m);
     const std::string decl = "    " + ind + T + " v" + std::to_string(m) + (L ? "[" + std::to_string(vec) + "]" : "");
@@ -420,15 +445,55 @@ struct Gen {
     os << "  }\n}\n";
   }
 
-  // Row reduce over group 1 of [P, Q].
+  // Marks in `need` the nodes an expression rooted at `m` recomputes inside
+  // a walk along the row: those varying along it, up to (not into) values
+  // that are constant per row (hoisted nodes and row reductions).
+  void mark_row_nodes(int m, std::vector<char>& need) const {
+    if (need[m] || !varies[m][p.G - 1]) return;
+    const lmpb_fnode& nd = h.nodes[m];
+    if (nd.kind == LMPB_FN_ROWRED) return;
+    need[m] = 1;
+    if (nd.kind == LMPB_FN_BINARY) {
+      mark_row_nodes(nd.a, need);
+      mark_row_nodes(nd.b, need);
+    } else if (nd.kind == LMPB_FN_UNARY) {
+      mark_row_nodes(nd.a, need);
+    }
+  }
+
+  // Row reduce over group 1 of [P, Q]: one warp (short rows) or CTA per row.
+  // In-kernel row reductions (LMPB_FN_ROWRED, e.g. the max and the sum of a
+  // softmax) run as walks along the row before the final one, each followed
+  // by the same warp/CTA tree as a reduce output and broadcast to the row's
+  // threads, so a fused value equals the separately realized reduction bit
+  // for bit.  Nodes constant along the row are computed once per row, as
+  // soon as the row reductions they read are known.
   void gen_row_reduce(const std::string& name) {
     prologue(name);
     const int64_t P = p.size[0], Q = p.size[1];
     const bool W = p.warp_rows;
     const std::string tpr = W ? "32u" : std::to_string(kThreads) + "u";
+    const int NN = (int)h.nodes.size();
     for (size_t j = 0; j < h.outs.size(); ++j)
       if (p.out_mode[j] >= LMPB_OUT_REDUCE_SUM)
         os << "  __shared__ " << tname(h.outs[j].dtype) << " sred" << j << "[" << kThreads / 32 << "];\n";
+    std::vector<int> rr;  // row reductions in order
+    std::vector<int> phase(NN, 0);
+    for (int m = 0; m < NN; ++m) {
+      const lmpb_fnode& nd = h.nodes[m];
+      if (nd.kind == LMPB_FN_ROWRED) {
+        rr.push_back(m);
+        phase[m] = (int)rr.size();
+        if (!W) {
+          const std::string T = tname(nd.dtype);
+          os << "  __shared__ " << T << " srr" << m << "[" << kThreads / 32 << "];\n  __shared__ " << T << " sbc" << m << ";\n";
+        }
+      } else if (nd.kind == LMPB_FN_BINARY) {
+        phase[m] = std::max(phase[nd.a], phase[nd.b]);
+      } else if (nd.kind == LMPB_FN_UNARY) {
+        phase[m] = phase[nd.a];
+      }
+    }
     os << "  const unsigned lane = threadIdx.x & 31u, wid = threadIdx.x >> 5;\n";
     if (W)
       os << "  for (" << I << " row = blockIdx.x * " << kThreads / 32 << "u + wid; row < " << P << "u; row += gridDim.x * " << kThreads / 32 << "u) {\n"
@@ -436,19 +501,76 @@ struct Gen {
     else
       os << "  for (" << I << " row = blockIdx.x; row < " << P << "u; row += gridDim.x) {\n"
          << "    const unsigned t = threadIdx.x;\n";
-    // per-row nodes (not varying along Q) first
     std::vector<std::string> coord = {"row", "q"};
     std::vector<std::string> loff(h.leaves.size());
     for (size_t i = 0; i < h.leaves.size(); ++i) loff[i] = leaf_offset((int)i, coord);
-    std::vector<char> done(h.nodes.size(), 0);
-    for (int m = 0; m < (int)h.nodes.size(); ++m)
-      if (!varies[m][1]) { emit_node(m, "", loff); done[m] = 1; }
+    std::vector<char> done(NN, 0);
+    auto hoist = [&](int upto) {  // per-row nodes whose row reductions are known
+      for (int m = 0; m < NN; ++m)
+        if (!done[m] && !varies[m][1] && h.nodes[m].kind != LMPB_FN_ROWRED && phase[m] <= upto) {
+          emit_node(m, "", loff);
+          done[m] = 1;
+        }
+    };
+    auto walk_open = [&]() {
+      if (p.row_unroll > 1) os << "    #pragma unroll " << p.row_unroll << "\n";
+      os << "    for (" << I << " q = t * " << vec << "u; q < " << Q << "u; q += " << tpr << " * " << vec << "u) {\n";
+    };
+    for (size_t k = 0; k < rr.size(); ++k) {
+      hoist((int)k);
+      const int r = rr[k];
+      const lmpb_fnode& nd = h.nodes[r];
+      const std::string T = tname(nd.dtype), a = "racc" + std::to_string(r);
+      const bool mx = nd.sub == LMPB_MAX;
+      const std::string ident = mx ? "lmpb_dev::lowest<" + T + ">()" : T + "(0)";
+      if (!varies[nd.a][1]) {  // a row reduction of a value constant along the row
+        os << "    " << T << " " << a << " = " << ident << ";\n";
+      } else {
+        os << "    " << T << " " << a << " = " << ident << ";\n";
+        std::vector<char> need(NN, 0);
+        mark_row_nodes(nd.a, need);
+        walk_open();
+        for (int m = 0; m < NN; ++m)
+          if (need[m]) emit_node(m, "  ", loff);
+        const std::string x = "static_cast<" + T + ">(" + ref(nd.a, vec > 1) + ")";
+        const std::string upd = mx ? a + " = (" + a + " < " + x + ") ? " + x + " : " + a + ";"
+                                   : a + " = lmpb_dev::r_add<" + T + ">(" + a + ", " + x + ");";
+        if (vec > 1)
+          os << "      #pragma unroll\n      for (int j = 0; j < " << vec << "; ++j) " << upd << "\n";
+        else
+          os << "      " << upd << "\n";
+        os << "    }\n";
+      }
+      if (!varies[nd.a][1]) {
+        // sum over Q copies, or the value itself for max: as the reduce
+        // output of a constant would compute it (a sequential walk per thread
+        // and the tree), recomputed here the same way
+        walk_open();
+        const std::string x = "static_cast<" + T + ">(" + ref(nd.a, false) + ")";
+        const std::string upd = mx ? a + " = (" + a + " < " + x + ") ? " + x + " : " + a + ";"
+                                   : a + " = lmpb_dev::r_add<" + T + ">(" + a + ", " + x + ");";
+        if (vec > 1) os << "      #pragma unroll\n      for (int j = 0; j < " << vec << "; ++j) " << upd << "\n";
+        else os << "      " << upd << "\n";
+        os << "    }\n";
+      }
+      const std::string red = mx ? "warp_max" : "warp_sum";
+      os << "    " << a << " = " << red << "(" << a << ");\n";
+      if (W) {
+        os << "    const " << T << " v" << r << " = __shfl_sync(0xffffffffu, " << a << ", 0);\n";
+      } else {
+        os << "    if (lane == 0) srr" << r << "[wid] = " << a << ";\n    __syncthreads();\n";
+        os << "    if (wid == 0) { " << a << " = lane < " << kThreads / 32 << "u ? srr" << r << "[lane] : " << ident << "; "
+           << a << " = " << red << "(" << a << "); if (lane == 0) sbc" << r << " = " << a << "; }\n    __syncthreads();\n";
+        os << "    const " << T << " v" << r << " = sbc" << r << ";\n    __syncthreads();\n";
+      }
+      done[r] = 1;
+    }
+    hoist((int)rr.size());
     for (size_t j = 0; j < h.outs.size(); ++j)
       if (p.out_mode[j] >= LMPB_OUT_REDUCE_SUM)
         os << "    " << tname(h.outs[j].dtype) << " acc" << j << " = 0;\n";
-    if (p.row_unroll > 1) os << "    #pragma unroll " << p.row_unroll << "\n";
-    os << "    for (" << I << " q = t * " << vec << "u; q < " << Q << "u; q += " << tpr << " * " << vec << "u) {\n";
-    for (int m = 0; m < (int)h.nodes.size(); ++m)
+    walk_open();
+    for (int m = 0; m < NN; ++m)
       if (!done[m]) emit_node(m, "  ", loff);
     emit_full_outputs("  ", "row * " + std::to_string(Q) + "u + q");
     for (size_t j = 0; j < h.outs.size(); ++j) {
@@ -595,6 +717,9 @@ std::string generate(lmpb_fused_s& h) {
   src << "template <typename T> __device__ __forceinline__ T warp_sum(T v) {\n"
          "  #pragma unroll\n  for (int d = 16; d > 0; d >>= 1) v = lmpb_dev::r_add<T>(v, static_cast<T>(__shfl_down_sync(0xffffffffu, v, d)));\n"
          "  return v;\n}\n";
+  src << "template <typename T> __device__ __forceinline__ T warp_max(T v) {\n"
+         "  #pragma unroll\n  for (int d = 16; d > 0; d >>= 1) { T o = static_cast<T>(__shfl_down_sync(0xffffffffu, v, d)); v = (v < o) ? o : v; }\n"
+         "  return v;\n}\n";
   src << "template <> __device__ __forceinline__ bool warp_sum<bool>(bool v) { return __any_sync(0xffffffffu, v); }\n";
   src << "template <> __device__ __forceinline__ short warp_sum<short>(short v) { int x = v;\n"
          "  for (int d = 16; d > 0; d >>= 1) x = (short)(x + __shfl_down_sync(0xffffffffu, x, d)); return (short)x; }\n";
@@ -698,6 +823,7 @@ lmpb_status compile(const std::string& src, std::shared_ptr<Cubin>& out) {
     out = c;
     return LMPB_OK;
   }
+  if (getenv("LMPB_FUSED_LOG")) fprintf(stderr, "[lmpb fused] NVRTC compile %s (%zu bytes of source)\n", hex, src.size());
   nvrtcProgram prog;
   if (nvrtcCreateProgram(&prog, src.c_str(), "lmpb_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
     return set_error(LMPB_ERR_COMPILE, "nvrtcCreateProgram failed");
@@ -830,6 +956,10 @@ extern "C" lmpb_status lmpb_fused_build(const lmpb_fnode* nodes, int n_nodes, co
       case LMPB_FN_UNARY:
         if (nd.sub < LMPB_NEG || nd.sub > LMPB_CLAMP || nd.a < 0 || nd.a >= m)
           return set_error(LMPB_ERR_INVALID, "fused: bad unary node");
+        break;
+      case LMPB_FN_ROWRED:
+        if ((nd.sub != LMPB_SUM && nd.sub != LMPB_MAX) || nd.a < 0 || nd.a >= m)
+          return set_error(LMPB_ERR_INVALID, "fused: bad row-reduction node");
         break;
       default: return set_error(LMPB_ERR_INVALID, "fused: unknown node kind");
     }

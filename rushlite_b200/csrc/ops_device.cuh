@@ -42,6 +42,16 @@ __device__ __forceinline__ double m_cos(double a) { return cos(a); }
 __device__ __forceinline__ float m_tan(float a) { return tanf(a); }
 __device__ __forceinline__ double m_tan(double a) { return tan(a); }
 
+// Smallest finite value of T: the identity of a max reduction (the
+// numeric_limits<T>::lowest() the eager reductions start from).
+template <typename T> __device__ __forceinline__ T lowest();
+template <> __device__ __forceinline__ bool lowest<bool>() { return false; }
+template <> __device__ __forceinline__ short lowest<short>() { return (short)-32768; }
+template <> __device__ __forceinline__ int lowest<int>() { return -2147483647 - 1; }
+template <> __device__ __forceinline__ long long lowest<long long>() { return -9223372036854775807ll - 1; }
+template <> __device__ __forceinline__ float lowest<float>() { return -3.40282346638528859812e+38f; }
+template <> __device__ __forceinline__ double lowest<double>() { return -1.79769313486231570815e+308; }
+
 template <typename T> __device__ __forceinline__ T r_add(T a, T b) { return a + b; }
 template <typename T> __device__ __forceinline__ T r_sub(T a, T b) { return a - b; }
 template <typename T> __device__ __forceinline__ T r_mul(T a, T b) { return a * b; }

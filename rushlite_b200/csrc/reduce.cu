@@ -74,54 +74,50 @@ struct V16 {
 };
 
 // Reduces `len` contiguous elements starting at `row` with the threads
-// [lane0, lane0 + nthreads); returns the per-thread partial.
-template <int OP, typename T, bool VEC>
-__device__ __forceinline__ T row_partial(const T* __restrict__ row, int64_t len, int tid,
-                                         int nthreads) {
+// [lane0, lane0 + nthreads); returns the per-thread partial.  The row is cut
+// into packets of PW contiguous elements; thread `tid` takes packets tid,
+// tid + nthreads, ... and folds each packet's elements in order.  This is the
+// walk of the fused compiler's row reductions (csrc/fused.cpp, packet width
+// `vec`), so an eager last-axis sum and a fused one add in the same order.
+template <typename T, int PW>
+struct alignas(PW * sizeof(T) >= 16 ? 16 : PW * sizeof(T)) RowPack {
+  T v[PW];
+};
+
+template <int OP, typename T, int PW>
+__device__ __forceinline__ T row_partial(const T* __restrict__ row, int64_t len, int tid, int nthreads) {
   using R = RedOp<OP, T>;
+  using Pk = RowPack<T, PW>;
   T acc = R::identity();
-  if constexpr (VEC) {
-    constexpr int N = V16<T>::N;
-    const uint4* r4 = reinterpret_cast<const uint4*>(row);
-    const int64_t nv = len / N;
-    int64_t i = tid;
-    for (; i + 3 * nthreads < nv; i += 4 * nthreads) {
-      V16<T> x0, x1, x2, x3;
-      x0.raw = __ldg(r4 + i);
-      x1.raw = __ldg(r4 + i + nthreads);
-      x2.raw = __ldg(r4 + i + 2 * nthreads);
-      x3.raw = __ldg(r4 + i + 3 * nthreads);
+  const Pk* pk = reinterpret_cast<const Pk*>(row);
+  const int64_t np = len / PW;  // len % PW == 0 (the host picks PW so)
+  int64_t i = tid;
+  for (; i + 3 * nthreads < np; i += 4 * nthreads) {
+    Pk x[4];
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc = R::apply(acc, x0.v[j]);
+    for (int u = 0; u < 4; ++u) x[u] = pk[i + u * nthreads];
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc = R::apply(acc, x1.v[j]);
+    for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc = R::apply(acc, x2.v[j]);
+      for (int j = 0; j < PW; ++j) acc = R::apply(acc, x[u].v[j]);
+  }
+  for (; i < np; i += nthreads) {
+    const Pk x = pk[i];
 #pragma unroll
-      for (int j = 0; j < N; ++j) acc = R::apply(acc, x3.v[j]);
-    }
-    for (; i < nv; i += nthreads) {
-      V16<T> x;
-      x.raw = __ldg(r4 + i);
-#pragma unroll
-      for (int j = 0; j < N; ++j) acc = R::apply(acc, x.v[j]);
-    }
-    for (int64_t t = nv * N + tid; t < len; t += nthreads) acc = R::apply(acc, row[t]);
-  } else {
-    for (int64_t t = tid; t < len; t += nthreads) acc = R::apply(acc, row[t]);
+    for (int j = 0; j < PW; ++j) acc = R::apply(acc, x.v[j]);
   }
   return acc;
 }
 
 // One CTA per row (grid-stride over rows).
-template <int OP, typename T, bool VEC>
+template <int OP, typename T, int PW>
 __global__ void __launch_bounds__(kThreads)
     reduce_rows_cta_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t rows,
                            int64_t len) {
   __shared__ T warp_part[kThreads / 32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    T acc = row_partial<OP, T, VEC>(in + r * len, len, threadIdx.x, kThreads);
+    T acc = row_partial<OP, T, PW>(in + r * len, len, threadIdx.x, kThreads);
     acc = warp_reduce<OP, T>(acc);
     if (lane == 0) warp_part[wid] = acc;
     __syncthreads();
@@ -135,7 +131,7 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // One warp per row.
-template <int OP, typename T, bool VEC>
+template <int OP, typename T, int PW>
 __global__ void __launch_bounds__(kThreads)
     reduce_rows_warp_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t rows,
                             int64_t len) {
@@ -143,7 +139,7 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t warps = (int64_t)gridDim.x * (kThreads / 32);
   for (int64_t r = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); r < rows;
        r += warps) {
-    T acc = row_partial<OP, T, VEC>(in + r * len, len, lane, 32);
+    T acc = row_partial<OP, T, PW>(in + r * len, len, lane, 32);
     acc = warp_reduce<OP, T>(acc);
     if (lane == 0) out[r] = acc;
   }
@@ -399,17 +395,26 @@ static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, c
     return launch_status("fill_identity_kernel");
   }
   if (p.inner == 1) {
-    constexpr int N = V16<T>::N;
-    const bool vec = (p.R % N == 0) && aligned16(in);
+    // packet width as the fused compiler picks it for a row reduction: the
+    // largest of 8, 4, 2 dividing the row, when input and output are 16-byte
+    // aligned; otherwise one element
+    int pw = 1;
+    if (aligned16(in) && aligned16(out))
+      for (int w = 8; w > 1; w >>= 1)
+        if (p.R % w == 0) { pw = w; break; }
     const int64_t cap = (int64_t)sm_count() * 8;
-    if (p.R >= 2048) {
-      int grid = (int)std::min<int64_t>(p.outer, cap);
-      if (vec) reduce_rows_cta_kernel<OP, T, true><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
-      else reduce_rows_cta_kernel<OP, T, false><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
-    } else {
-      int grid = (int)std::min<int64_t>((p.outer + 7) / 8, cap);
-      if (vec) reduce_rows_warp_kernel<OP, T, true><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
-      else reduce_rows_warp_kernel<OP, T, false><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+    const bool cta = p.R >= 2048;
+    const int grid = (int)(cta ? std::min<int64_t>(p.outer, cap) : std::min<int64_t>((p.outer + 7) / 8, cap));
+    auto launch = [&](auto pw_c) {
+      constexpr int PW = decltype(pw_c)::value;
+      if (cta) reduce_rows_cta_kernel<OP, T, PW><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+      else reduce_rows_warp_kernel<OP, T, PW><<<grid, kThreads, 0, st>>>(in, out, p.outer, p.R);
+    };
+    switch (pw) {
+      case 8: launch(std::integral_constant<int, 8>{}); break;
+      case 4: launch(std::integral_constant<int, 4>{}); break;
+      case 2: launch(std::integral_constant<int, 2>{}); break;
+      default: launch(std::integral_constant<int, 1>{}); break;
     }
     return launch_status("reduce_rows_kernel");
   }

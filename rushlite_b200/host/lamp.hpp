@@ -95,7 +95,7 @@ using ImplPtr = std::shared_ptr<TensorImpl>;
 // with the bias and clamp in its epilogue; read any other way it realizes as
 // a plain GEMM.
 struct LazyNode {
-  enum Kind { kBinary, kUnary, kConst, kReduceSum, kMatmul };
+  enum Kind { kBinary, kUnary, kConst, kReduceSum, kMatmul, kReduceMax };
   Kind kind;
   int op = 0;
   double p0 = 0.0, p1 = 0.0;  // clamp bounds / constant value

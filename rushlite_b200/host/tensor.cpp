@@ -281,7 +281,8 @@ static bool in_place_safe(const TensorImpl* t, const StorageImpl* dst, const std
   if (!seen.insert(key).second) return true;
   if (t->storage.get() == dst) return elementwise && !t->lazy && t->shape == shape;
   if (!t->lazy) return true;
-  const bool ew = elementwise && t->lazy->kind != LazyNode::kMatmul && t->lazy->kind != LazyNode::kReduceSum;
+  const bool ew = elementwise && t->lazy->kind != LazyNode::kMatmul && t->lazy->kind != LazyNode::kReduceSum &&
+                  t->lazy->kind != LazyNode::kReduceMax;
   for (const auto& in : t->lazy->inputs)
     if (!in_place_safe(in.get(), dst, shape, seen, ew)) return false;
   return true;
@@ -549,6 +550,19 @@ static ImplPtr record(LazyNode::Kind kind, int op, std::vector<ImplPtr> inputs, 
 
 namespace {
 
+bool gemm_epilogue_root(const TensorImpl* t);
+
+// Size of the pending graph under `t`, counted up to `cap`.
+size_t pending_size(const TensorImpl* t, size_t cap, std::unordered_set<const TensorImpl*>& seen) {
+  if (!t->lazy || !seen.insert(t).second) return 0;
+  size_t n = 1;
+  for (const auto& in : t->lazy->inputs) {
+    if (n >= cap) break;
+    n += pending_size(in.get(), cap - n, seen);
+  }
+  return n;
+}
+
 struct ProgramBuilder {
   std::vector<lmpb_fnode> nodes;
   std::vector<lmpb_fleaf> leaves;
@@ -559,6 +573,7 @@ struct ProgramBuilder {
   std::map<std::tuple<const void*, int, std::vector<size_t>>, int> leaf_memo;
   std::string sig;  // compact binary signature of the program (cache key)
   size_t budget = 480;
+  std::vector<size_t> iter;  // iteration space (when known): enables in-kernel row reductions
 
   template <typename T>
   void put(const T& v) {
@@ -615,7 +630,8 @@ struct ProgramBuilder {
   static bool invariant_along(TensorImpl* t, const std::vector<size_t>& full, const std::vector<size_t>& target,
                               std::unordered_set<TensorImpl*>& seen) {
     if (!seen.insert(t).second) return true;
-    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul) {
+    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul ||
+        t->lazy->kind == LazyNode::kReduceMax) {
       const size_t nd = full.size();
       for (size_t k = 0; k < nd; ++k) {
         const size_t d = nd - 1 - k;
@@ -628,6 +644,18 @@ struct ProgramBuilder {
     for (const auto& in : t->lazy->inputs)
       if (!invariant_along(in.get(), full, target, seen)) return false;
     return true;
+  }
+
+  // True when pending reduction `t` reduces only the last axis of this
+  // program's iteration space (its input has the iteration shape).
+  bool row_reduction(const TensorImpl* t) const {
+    const TensorImpl* x = t->lazy->inputs[0].get();
+    const size_t nd = iter.size();
+    if (nd == 0 || x->shape != iter || iter[nd - 1] <= 1 || t->shape.size() != nd || t->dtype != x->dtype)
+      return false;
+    for (size_t d = 0; d + 1 < nd; ++d)
+      if (t->shape[d] != iter[d]) return false;
+    return t->shape[nd - 1] == 1;
   }
 
   int visit(TensorImpl* t) {
@@ -662,8 +690,32 @@ struct ProgramBuilder {
         return id;
       }
     }
-    if (!t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul ||
-        nodes.size() > budget) {
+    if (t->lazy && (t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kReduceMax) &&
+        nodes.size() <= budget && row_reduction(t)) {
+      // a keep-dim sum / max over the last axis of this program's own space
+      // (a softmax's max and sum): computed inside the kernel, per row
+      lmpb_fnode n{};
+      n.kind = LMPB_FN_ROWRED;
+      n.sub = t->lazy->kind == LazyNode::kReduceMax ? LMPB_MAX : LMPB_SUM;
+      n.dtype = (int)t->dtype;
+      n.a = visit(t->lazy->inputs[0].get());
+      id = add_node(n);
+      memo[t] = id;
+      return id;
+    }
+    // Realized first, then read as a leaf: barriers (reductions the kernel
+    // cannot place, matmuls); a Linear (matmul + bias [+ clamp]), which runs
+    // as one GEMM with the bias and clamp in its epilogue; an operand smaller
+    // than the iteration space with a long pending history (e.g. a parameter
+    // updated lazily step after step), which inlined would be recomputed for
+    // every element and grow the program every step; oversize graphs.
+    bool materialise = !t->lazy || t->lazy->kind == LazyNode::kReduceSum || t->lazy->kind == LazyNode::kMatmul ||
+                       t->lazy->kind == LazyNode::kReduceMax || nodes.size() > budget || gemm_epilogue_root(t);
+    if (!materialise && !iter.empty() && t->shape != iter) {
+      std::unordered_set<const TensorImpl*> seen;
+      materialise = pending_size(t, 17, seen) > 16;
+    }
+    if (materialise) {
       id = leaf(t);  // realizes barriers / oversize sub-graphs first
     } else {
       LazyNode& L = *t->lazy;
@@ -743,6 +795,9 @@ lmpb_status run_program(ProgramBuilder& pb, const std::vector<size_t>& iter) {
     if (it != prog_cache().end()) h = it->second;
   }
   if (!h) {
+    static const bool log = getenv("LMPB_FUSED_LOG") != nullptr;
+    if (log) fprintf(stderr, "[lmpb fused] new program: %zu nodes, %zu leaves, %zu outputs\n", pb.nodes.size(),
+                     pb.leaves.size(), pb.outs.size());
     std::vector<int64_t> it64 = to_i64(iter);
     lmpb_status st = lmpb_fused_build(pb.nodes.data(), (int)pb.nodes.size(), pb.leaves.data(), (int)pb.leaves.size(),
                                       pb.outs.data(), (int)pb.outs.size(), it64.data(), (int)it64.size(), &h);
@@ -814,6 +869,7 @@ void run_requests(std::vector<Request>& reqs) {
   for (const auto& iter : order) {
     auto& g = groups[iter];
     ProgramBuilder pb;
+    pb.iter = iter;
     for (Request* r : g) {
       const int node = r->chain.empty() ? pb.visit(r->expr.get()) : pb.chain(r->chain, r->target->dtype);
       const int addend = r->addend.empty() ? -1 : pb.chain(r->addend, r->target->dtype);
@@ -826,6 +882,7 @@ void run_requests(std::vector<Request>& reqs) {
       for (Request* r : g) {
         if (r->mode < LMPB_OUT_REDUCE_SUM) {
           ProgramBuilder p1;
+          p1.iter = iter;
           int node = r->chain.empty() ? p1.visit(r->expr.get()) : -1;
           if (node < 0) {
             node = p1.visit(r->chain[0].get());
@@ -851,6 +908,7 @@ void run_requests(std::vector<Request>& reqs) {
           }
           ImplPtr full = new_impl(iter, r->target->dtype, DeviceType::CUDA, true);
           ProgramBuilder p1;
+          p1.iter = iter;
           const int rn = r->chain.empty() ? p1.visit(r->expr.get()) : p1.chain(r->chain, r->target->dtype);
           p1.output(rn, LMPB_OUT_STORE, full->dtype, iter, full->storage->ptr);
           LMPB_OK_OR_THROW(run_program(p1, iter));
@@ -901,6 +959,27 @@ void run_matmul(TensorImpl* dst, TensorImpl* M, const EpilogueSpec* ep) {
 // t = clamp(M + bias, lo, hi) or t = M + bias, with M a pending fp32 matmul
 // [m,n] and bias an fp32 row of n ([n] or [1,n]): one GEMM with the epilogue.
 // M itself stays pending (it realizes as a plain GEMM if it is ever read).
+// True when pending `t` is one of the GEMM-epilogue patterns gemm_epilogue
+// realizes as one GEMM: matmul + bias row, or clamp(matmul + bias row).
+bool gemm_epilogue_root(const TensorImpl* t) {
+  if (!t->lazy || t->dtype != DataType::Float32 || t->shape.size() != 2 || t->storage) return false;
+  const TensorImpl* add = t;
+  if (t->lazy->kind == LazyNode::kUnary && t->lazy->op == LMPB_CLAMP) add = t->lazy->inputs[0].get();
+  if (!add->lazy || add->storage || add->lazy->kind != LazyNode::kBinary || add->lazy->op != LMPB_ADD ||
+      add->dtype != DataType::Float32 || add->shape != t->shape)
+    return false;
+  const size_t n = t->shape[1];
+  for (int s = 0; s < 2; ++s) {
+    const TensorImpl* M = add->lazy->inputs[s].get();
+    const TensorImpl* b = add->lazy->inputs[1 - s].get();
+    const bool row = b->shape == std::vector<size_t>{n} || b->shape == std::vector<size_t>{1, n};
+    if (M->lazy && M->lazy->kind == LazyNode::kMatmul && !M->storage && M->shape == t->shape &&
+        b->dtype == DataType::Float32 && row)
+      return true;
+  }
+  return false;
+}
+
 bool gemm_epilogue(const ImplPtr& t) {
   if (t->dtype != DataType::Float32 || t->shape.size() != 2 || t->storage) return false;
   const size_t n = t->shape[1];
@@ -963,6 +1042,15 @@ void realize_all(const std::vector<ImplPtr>& ts) {
     }
     if (L->kind == LazyNode::kMatmul) {
       run_matmul(t.get(), nullptr, nullptr);
+      continue;
+    }
+    if (L->kind == LazyNode::kReduceMax) {  // read on its own: the eager kernel
+      TensorImpl* x = L->inputs[0].get();
+      const void* px = x->data();
+      std::vector<int64_t> s64 = to_i64(x->shape);
+      LMPB_OK_OR_THROW(lmpb_reduce(LMPB_MAX, (int)x->dtype, px, s64.data(), (int)s64.size(), (int)s64.size() - 1,
+                                   t->storage->ptr, g_stream));
+      t->lazy = nullptr;
       continue;
     }
     if (L->kind == LazyNode::kReduceSum) {
@@ -1118,8 +1206,31 @@ static Tensor reduce(int op, const Tensor& a, size_t axis) {
   return Tensor(out);
 }
 
-Tensor sum(const Tensor& a, size_t axis) { return reduce(LMPB_SUM, a, axis); }
-Tensor max(const Tensor& a, size_t axis) { return reduce(LMPB_MAX, a, axis); }
+// Under capture a float sum or max over the last axis stays pending, so that
+// the kernel reading it computes it per row (softmax: max, exp, sum, divide
+// and what follows in one pass); read on its own it runs the same row walk
+// and tree as the eager kernel (equal bit for bit).
+static bool lazy_row_reduction(const Tensor& a, size_t axis) {
+  return a.device() == DeviceType::CUDA && lazy::should_capture(a.device()) && axis + 1 == a.shape().size() &&
+         a.shape()[axis] > 1 && (a.type() == DataType::Float32 || a.type() == DataType::Float64);
+}
+
+Tensor sum(const Tensor& a, size_t axis) {
+  if (lazy_row_reduction(a, axis)) {
+    std::vector<size_t> os = a.shape();
+    os[axis] = 1;
+    return Tensor(record(LazyNode::kReduceSum, LMPB_SUM, {a.impl()}, os, a.type()));
+  }
+  return reduce(LMPB_SUM, a, axis);
+}
+Tensor max(const Tensor& a, size_t axis) {
+  if (lazy_row_reduction(a, axis)) {
+    std::vector<size_t> os = a.shape();
+    os[axis] = 1;
+    return Tensor(record(LazyNode::kReduceMax, LMPB_MAX, {a.impl()}, os, a.type()));
+  }
+  return reduce(LMPB_MAX, a, axis);
+}
 Tensor min(const Tensor& a, size_t axis) { return reduce(LMPB_MIN, a, axis); }
 Tensor prod(const Tensor& a, size_t axis) { return reduce(LMPB_PROD, a, axis); }
 
