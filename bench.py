@@ -323,6 +323,42 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
                                      "frac": value / world / peak, "peak_source": src, "per": "GPU"}}
 
 
+def workload_c2eager(rsl, torch, args):
+    """The C2 forward issued op by op without capture: the eager elementwise
+    kernels one at a time (same-shape binary, broadcast binary, unary) on
+    [8192, 8192] fp32, each timed with CUDA events; GB/s = bytes the op must
+    move (inputs read once, output written once) / time."""
+    R, Cn = 8192, 8192
+    rng = np.random.default_rng(1234)
+    a = rsl.Variable(rng.random((R, Cn), dtype=np.float32))
+    b = rsl.Variable(rng.random((R, 1), dtype=np.float32))
+    big, col = R * Cn * 4, R * 4
+    aa = a * a
+    c = aa + b
+    x = rsl.exp(c)
+    e = x * a
+    lg = rsl.log(b + 1.0)
+    ops = {
+        "mul_same_shape": (lambda: (a * a).realize(), 3 * big),
+        "add_broadcast_col": (lambda: (aa + b).realize(), 2 * big + col),
+        "exp_unary": (lambda: rsl.exp(c).realize(), 2 * big),
+        "sub_broadcast_col": (lambda: (e - lg).realize(), 2 * big + col),
+    }
+    res, tot_b, tot_ms = {}, 0, 0.0
+    for name, (fn, nbytes) in ops.items():
+        ms = _time(torch, fn, max(10, min(args.steps, 200)))
+        res[name] = {"ms": ms, "GB/s": nbytes / ms / 1e6}
+        tot_b += nbytes
+        tot_ms += ms
+    peak, src = peak_hbm()
+    value = tot_b / tot_ms / 1e6
+    return {"metric": "eager elementwise HBM GB/s (C2 ops issued one by one, no capture)", "value": value,
+            "unit": "GB/s", "higher_is_better": True, "dtype": "f32",
+            "config": {"workload": "C2 forward ops, eager", "a": [R, Cn], "b": [R, 1]}, "ops": res,
+            "roofline": {"bound": "hbm", "achieved": value, "peak": peak, "unit": "GB/s", "frac": value / peak,
+                         "peak_source": src}}
+
+
 def workload_c4(rsl, torch, args):
     """fp32 matmul sweep through the public API, forward and dA/dB (3 GEMMs, 6MNK flops)."""
     out, tot_f, tot_ms = {}, 0.0, 0.0
@@ -422,7 +458,7 @@ def _mlp_step_dp(rsl, ps, x, y, lr, D=None):
         m = rsl.max(h, 1)
         e = rsl.exp(h - m)
         p = e / rsl.sum(e, 1)
-    loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
+        loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
     loss.backward()
     if D is not None:
         D.all_reduce_many([q.grad for q in ps[1::2]], "sum", overlap=True)
@@ -546,7 +582,7 @@ def _mlp_step_inplace(rsl, ps, x, y, lr):
         m = rsl.max(h, 1)
         e = rsl.exp(h - m)
         p = e / rsl.sum(e, 1)
-    loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
+        loss = rsl.sum(rsl.sum(-y * rsl.log(p + 1e-3), 1), 0)
     loss.backward()
     with rsl.no_grad(), rsl.capture_on():
         for q in ps:
@@ -726,7 +762,7 @@ def run_secondary(rsl, torch, args, rank, world, pg, local):
     (at N = 1) CPU baseline.  At N > 1: C3 (row-sharded, the dim-0 partials
     all-reduced) and C5 (data parallel, gradient all-reduce); C4 and C1 are
     single-GPU configs."""
-    names = ["c3", "c4", "c5", "c1"] if world == 1 else ["c3", "c5"]
+    names = ["c3", "c4", "c5", "c1", "c2eager"] if world == 1 else ["c3", "c5"]
     cpu = {"c3": cpu_baseline_c3, "c4": cpu_baseline_c4, "c5": cpu_baseline_c5, "c1": cpu_baseline_c1}
     blocks = {}
     for name in names:
@@ -743,6 +779,8 @@ def run_secondary(rsl, torch, args, rank, world, pg, local):
                 blk = workload_c5(rsl, torch, args, rank, world, pg)
             elif name == "c4":
                 blk = workload_c4(rsl, torch, args)
+            elif name == "c2eager":
+                blk = workload_c2eager(rsl, torch, args)
             else:
                 blk = workload_c1(rsl, torch, args)
         except Exception as e:  # a secondary block must never sink the headline line
@@ -752,7 +790,7 @@ def run_secondary(rsl, torch, args, rank, world, pg, local):
         if wall1 - wall0 < 1.0:
             time.sleep(1.0 - (wall1 - wall0))
         blk["clocks"] = clocks.stop(*(args.timed_window or (wall0, wall1)))
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and name in cpu:
             try:
                 blk["cpu_baseline"] = cpu[name]()
             except Exception as e:
@@ -779,7 +817,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--batch", type=int, default=8192, help="C5 global batch (8192 = the config)")
     ap.add_argument("--rows", type=int, default=8192, help="rows of a (8192 = the C2 config; smaller for profiling)")
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"],
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c2eager"],
                     help="c2 (default) is the headline; the others are the secondary BASELINE configs")
     args = ap.parse_args()
     set_rows(args.rows)
@@ -815,7 +853,7 @@ def main():
             line = workload_c3(rsl, torch, args, rank, world)
         elif rank == 0:
             l0 = rsl.cuda.kernel_launches()
-            line = {"c1": workload_c1, "c4": workload_c4}[args.workload](rsl, torch, args)
+            line = {"c1": workload_c1, "c4": workload_c4, "c2eager": workload_c2eager}[args.workload](rsl, torch, args)
             line["gpu_launches_total"] = int(rsl.cuda.kernel_launches() - l0)
         # the timed loop when the workload reports it, else the whole workload
         clk = clocks.stop(*getattr(args, "timed_window", (wall0, time.time())))
