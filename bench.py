@@ -339,7 +339,7 @@ def workload_c2eager(rsl, torch, args):
     e = x * a
     lg = rsl.log(b + 1.0)
     ops = {
-        "mul_same_shape": (lambda: (a * a).realize(), 3 * big),
+        "mul_same_shape": (lambda: (a * a).realize(), 2 * big),  # a * a: one operand, read once
         "add_broadcast_col": (lambda: (aa + b).realize(), 2 * big + col),
         "exp_unary": (lambda: rsl.exp(c).realize(), 2 * big),
         "sub_broadcast_col": (lambda: (e - lg).realize(), 2 * big + col),
