@@ -19,6 +19,7 @@
 // sum differs from the reference's sequential order only by rounding.
 #include <cooperative_groups.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <limits>
 
@@ -217,12 +218,12 @@ int cluster_chunks() {
   return (e && atoi(e) == 16) ? 16 : kClusterChunks;
 }
 
-template <int OP, typename T, int VW, int CC>
+template <int OP, typename T, int VW, int CC, int CTX = 16, int DEPTH = 4>
 __global__ void __launch_bounds__(kThreads)
     reduce_cols_cluster_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t R, int64_t inner,
                                int64_t rows_per_chunk) {
   namespace cg = cooperative_groups;
-  constexpr int CTX = 16, CTY = kThreads / CTX;
+  constexpr int CTY = kThreads / CTX;
   using Rd = RedOp<OP, T>;
   __shared__ T part[CTY][CTX * VW];
   __shared__ T fin[CTX * VW];
@@ -237,12 +238,12 @@ __global__ void __launch_bounds__(kThreads)
   if (c < inner) {
     const T* base = in + (o * R) * inner + c;
     int64_t r = r0 + ty;
-    for (; r + 3 * CTY < r1; r += 4 * CTY) {
-      V16<T> x[4];
+    for (; r + (DEPTH - 1) * CTY < r1; r += DEPTH * CTY) {
+      V16<T> x[DEPTH];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u * CTY) * inner));
+      for (int u = 0; u < DEPTH; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u * CTY) * inner));
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < DEPTH; ++u)
 #pragma unroll
         for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
     }
@@ -361,6 +362,7 @@ struct ReducePlan {
   int vw;     // column vector width
   int ctx;    // column threads per CTA
   bool cluster;  // the chunks are one thread-block cluster (S = kClusterChunks, no workspace)
+  int cfg = 0;   // cluster kernel variant: bit 0 = 8 column threads, bit 1 = 8 rows in flight
   size_t ws_bytes;
 };
 
@@ -376,6 +378,10 @@ static ReducePlan plan_reduce(const void* in, const void* out, int64_t outer, in
     // the cluster instead of through a workspace and a second kernel
     const int64_t colblocks = (inner / p.vw + 15) / 16;
     const char* e = getenv("LMPB_REDUCE_CLUSTER");  // A/B switch: 0 keeps the workspace path
+    if (const char* c2 = getenv("LMPB_REDUCE_CLUSTER_CFG")) {  // tuning override "ctx,depth": 8|16, 4|8
+      int cx = 16, dp = 4;
+      if (sscanf(c2, "%d,%d", &cx, &dp) == 2) p.cfg = (cx == 8 ? 1 : 0) + (dp == 8 ? 2 : 0);
+    }
     const int cc = cluster_chunks();
     if (p.S > 1 && p.vw == N && p.ctx == 16 && outer <= 65535 && R >= 16 * cc &&
         colblocks * outer * cc >= (int64_t)sm_count() * 2 && !(e && atoi(e) == 0)) {
@@ -437,7 +443,15 @@ static lmpb_status run_reduce(const ReducePlan& p, const T* in, T* out, T* ws, c
     cfg.attrs = at;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if (p.S == 16) {
+    if (p.cfg) {
+      const int64_t cb = (p.inner / p.vw + ((p.cfg & 1) ? 7 : 15)) / ((p.cfg & 1) ? 8 : 16);
+      cfg.gridDim = dim3((unsigned)cb, (unsigned)p.outer, (unsigned)p.S);
+      switch (p.cfg) {
+        case 1: e = cudaLaunchKernelEx(&cfg, reduce_cols_cluster_kernel<OP, T, N, kClusterChunks, 8, 4>, in, out, p.R, p.inner, rows_per_chunk); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, reduce_cols_cluster_kernel<OP, T, N, kClusterChunks, 16, 8>, in, out, p.R, p.inner, rows_per_chunk); break;
+        default: e = cudaLaunchKernelEx(&cfg, reduce_cols_cluster_kernel<OP, T, N, kClusterChunks, 8, 8>, in, out, p.R, p.inner, rows_per_chunk); break;
+      }
+    } else if (p.S == 16) {
       auto k = reduce_cols_cluster_kernel<OP, T, N, 16>;
       e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, k, in, out, p.R, p.inner, rows_per_chunk);
