@@ -303,6 +303,50 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// split_rows_kernel<true> for rows of at most NV * 1024 floats: the row is
+// read once into registers (NV 16-byte loads per thread, all in flight), its
+// max taken there, then split from the registers; same results.
+template <int NV>
+__global__ void __launch_bounds__(256)
+    split_rows_reg_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int64_t Kp, __half* __restrict__ hi,
+                          __half* __restrict__ lo, float* __restrict__ rowmax, int* __restrict__ expo) {
+  __shared__ float red[8];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4* row4 = reinterpret_cast<const float4*>(src + r * K);
+    float4 v[NV];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t c = threadIdx.x + i * 256;
+      v[i] = c * 4 < K ? __ldg(row4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      mx = fmaxf(fmaxf(mx, fmaxf(finite_abs(v[i].x), finite_abs(v[i].y))), fmaxf(finite_abs(v[i].z), finite_abs(v[i].w)));
+    mx = block_max256(mx, red);
+    const int e = row_exp(mx);
+    if (threadIdx.x == 0) {
+      rowmax[r] = mx;
+      expo[r] = e;
+    }
+    __half* hrow = hi + r * Kp;
+    __half* lrow = lo + r * Kp;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t c = threadIdx.x + i * 256;
+      if (c * 4 < Kp) {
+        __half h[4], l[4];
+        split16(pow2_scale(v[i].x, e), h[0], l[0]);
+        split16(pow2_scale(v[i].y, e), h[1], l[1]);
+        split16(pow2_scale(v[i].z, e), h[2], l[2]);
+        split16(pow2_scale(v[i].w, e), h[3], l[3]);
+        *reinterpret_cast<uint2*>(hrow + c * 4) = *reinterpret_cast<const uint2*>(h);
+        *reinterpret_cast<uint2*>(lrow + c * 4) = *reinterpret_cast<const uint2*>(l);
+      }
+    }
+  }
+}
+
 // src is [K, rows] row-major (the operand transposed): the finite max-abs of
 // every column r over K, as float bits into colmax[r] (zeroed beforehand;
 // non-negative floats order like their bits).  CTA = 64 columns x 256 k.
@@ -320,6 +364,55 @@ __global__ void __launch_bounds__(256)
   if (ty == 0 && r < rows) {
     mx = fmaxf(fmaxf(part[0][tx], part[1][tx]), fmaxf(part[2][tx], part[3][tx]));
     if (mx > 0.f) atomicMax(colmax + r, __float_as_uint(mx));
+  }
+}
+
+// colmax_kernel with 16-byte loads (rows % 4 == 0, src 16-byte aligned): a
+// CTA is 16 column quads (64 columns) x 16 k-lanes over 512 k, each thread
+// with 4 loads in flight.  Max is order-free, so the maxima are the same.
+constexpr int kColmaxK = 512;
+__global__ void __launch_bounds__(256)
+    colmax4_kernel(const float* __restrict__ src, int64_t rows, int64_t K, unsigned* __restrict__ colmax) {
+  __shared__ float4 part[16][16];
+  const int tq = threadIdx.x & 15, tk = threadIdx.x >> 4;
+  const int64_t r = (int64_t)blockIdx.x * 64 + 4 * tq;
+  const int64_t k0 = (int64_t)blockIdx.y * kColmaxK, k1 = k0 + kColmaxK < K ? k0 + kColmaxK : K;
+  float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (r < rows) {
+    const float* base = src + r;
+    int64_t k = k0 + tk;
+    for (; k + 48 < k1; k += 64) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(base + (k + 16 * u) * rows));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        m.x = fmaxf(m.x, finite_abs(v[u].x));
+        m.y = fmaxf(m.y, finite_abs(v[u].y));
+        m.z = fmaxf(m.z, finite_abs(v[u].z));
+        m.w = fmaxf(m.w, finite_abs(v[u].w));
+      }
+    }
+    for (; k < k1; k += 16) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(base + k * rows));
+      m.x = fmaxf(m.x, finite_abs(v.x));
+      m.y = fmaxf(m.y, finite_abs(v.y));
+      m.z = fmaxf(m.z, finite_abs(v.z));
+      m.w = fmaxf(m.w, finite_abs(v.w));
+    }
+  }
+  part[tk][tq] = m;
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    const int q = threadIdx.x >> 2, c = threadIdx.x & 3;
+    const int64_t col = (int64_t)blockIdx.x * 64 + threadIdx.x;
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 v = part[i][q];
+      mx = fmaxf(mx, c == 0 ? v.x : c == 1 ? v.y : c == 2 ? v.z : v.w);
+    }
+    if (col < rows && mx > 0.f) atomicMax(colmax + col, __float_as_uint(mx));
   }
 }
 
@@ -1028,7 +1121,13 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
                           __half* lo, float* rowmax, int* expo, cudaStream_t st) {
   if (kmajor) {
     const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(rows, (int64_t)sm_count() * 8));
-    if ((K & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0)
+    static const bool two_pass = getenv("LMPB_GEMM_SPLIT2PASS") != nullptr;  // A/B switch
+    const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+    if (vec && !two_pass && Kp <= 4096)
+      split_rows_reg_kernel<4><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
+    else if (vec && !two_pass && Kp <= 8192)
+      split_rows_reg_kernel<8><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
+    else if (vec)
       split_rows_kernel<true><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
     else
       split_rows_kernel<false><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
@@ -1037,8 +1136,13 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
   if ((Kp + 63) / 64 > 65535 || (K + 255) / 256 > 65535)
     return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
   const bool quad = (rows & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-  colmax_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + 255) / 256)), 256, 0, st>>>(
-      src, rows, K, reinterpret_cast<unsigned*>(rowmax));
+  static const bool scalar_colmax = getenv("LMPB_GEMM_COLMAX1") != nullptr;  // A/B switch
+  if (quad && !scalar_colmax)
+    colmax4_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + kColmaxK - 1) / kColmaxK)), 256, 0, st>>>(
+        src, rows, K, reinterpret_cast<unsigned*>(rowmax));
+  else
+    colmax_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + 255) / 256)), 256, 0, st>>>(
+        src, rows, K, reinterpret_cast<unsigned*>(rowmax));
   lmpb_status s = launch_status("gemm split pass (column maxima)");
   if (s != LMPB_OK) return s;
   const dim3 grid((unsigned)((rows + 63) / 64), (unsigned)((Kp + 63) / 64));
