@@ -49,6 +49,26 @@ METRIC = "fused elementwise/reduction HBM GB/s (C2 broadcast chain fwd+bwd)"
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 
 
+# The JSON line goes to the process's original stdout; everything else that
+# writes to file descriptor 1 (libraries such as NCCL printing their version)
+# is sent to stderr, so stdout carries exactly one line.
+_JSON_OUT = None
+
+
+def keep_stdout_for_json():
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line):
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -227,7 +247,7 @@ def run_reference_arm(args, rank, world):
                          "sample": f"{args.steps} steps of a [{rows}, {COLS}] row slice of C2 on the host CPU ({kind} CPU build)"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # --------------------------------------------------------------------------
@@ -823,6 +843,7 @@ def main():
     set_rows(args.rows)
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
+    keep_stdout_for_json()
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
@@ -861,7 +882,7 @@ def main():
             line["clocks"] = clk
             line.setdefault("n_gpus", world)
             line["data"] = "synthetic (seeded)"
-            print(json.dumps(line), flush=True)
+            emit(line)
         if pg:
             pg.destroy_process_group()
         return
@@ -1036,7 +1057,7 @@ def main():
             line["cpu_baseline"] = cpu_baseline(a_np, b_np)
         except Exception as e:  # the reported baseline must never sink the GPU line
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
-    print(json.dumps(line), flush=True)
+    emit(line)
     if pg:
         pg.destroy_process_group()
 
