@@ -274,6 +274,31 @@ lmpb_status lmpb_allreduce(int dtype, void* const* bufs, const int64_t* counts, 
                            void* stream);
 lmpb_status lmpb_comm_join(void* stream);
 
+/* Leading-axis reduction fused with the all-reduce of its result across the
+ * GPUs of a row-partitioned job, in ONE kernel over NVLink peer memory: each
+ * rank reduces its own rows (`in`, shape[ndim], along `axis` with all dims
+ * before it of extent 1), pushes its partial into every rank's exchange
+ * region, and every rank folds the partials in rank order, so all ranks write
+ * identical `out` (the reduction over all ranks' rows).  Replaces, for the
+ * sharded C3 dim-0 case, sum_cuda..prod_cuda (csrc/src/tensor/cuda/kernels.cu:112-122)
+ * followed by a separate all-reduce; the reference itself is single-device.
+ * Setup, once, collectively: every rank calls lmpb_peer_export (allocates its
+ * region, LMPB_PEER_HANDLE_BYTES of CUDA IPC handle out), the handles are
+ * exchanged out of band (rank order), then every rank calls lmpb_peer_import.
+ * Every rank must make the same sequence of lmpb_reduce_allreduce calls; the
+ * kernel waits for the other ranks with a bound (~2 s), after which it stops
+ * and lmpb_device_error reports LMPB_ERR_TIMEOUT.  One rank per GPU.
+ * LMPB_ERR_UNSUPPORTED when the shape is outside the fused path (the caller
+ * then reduces with lmpb_reduce and all-reduces with lmpb_allreduce). */
+#define LMPB_PEER_HANDLE_BYTES 64
+lmpb_status lmpb_peer_export(void* handle, size_t bytes);
+lmpb_status lmpb_peer_import(const void* handles, int nranks, int rank);
+lmpb_status lmpb_peer_close(void);
+/* Number of ranks of the peer context (0 when none is open). */
+int lmpb_peer_size(void);
+lmpb_status lmpb_reduce_allreduce(int op, int dtype, const void* in, const int64_t* shape, int ndim, int axis,
+                                  void* out, void* stream);
+
 /* ------------------------------------------------------ fused kernels */
 
 /* The lazy-fusion compiler behind capture_on / capture.  Replaces the NVRTC

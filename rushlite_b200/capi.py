@@ -43,7 +43,8 @@ EXPORTS = [
     "lmpb_fill", "lmpb_copy", "lmpb_add_inplace", "lmpb_fused_build", "lmpb_fused_launch",
     "lmpb_fused_release", "lmpb_fused_source", "lmpb_device_error", "lmpb_reduce_noalloc",
     "lmpb_gemm_f32_bias_act", "lmpb_comm_unique_id", "lmpb_comm_init", "lmpb_comm_destroy", "lmpb_comm_size",
-    "lmpb_allreduce", "lmpb_comm_join", "lmpb_gemm_sched_tile", "lmpb_gemm_sched_unit", "lmpb_gemm_sched_splits",
+    "lmpb_allreduce", "lmpb_comm_join", "lmpb_peer_export", "lmpb_peer_import", "lmpb_peer_close",
+    "lmpb_peer_size", "lmpb_reduce_allreduce", "lmpb_gemm_sched_tile", "lmpb_gemm_sched_unit", "lmpb_gemm_sched_splits",
 ]
 COMM_ID_BYTES = 128
 
@@ -108,6 +109,11 @@ def lib() -> C.CDLL:
         L.lmpb_comm_size.argtypes = []
         L.lmpb_allreduce.argtypes = [i32, C.POINTER(vp), P64, i32, i32, i32, vp]
         L.lmpb_comm_join.argtypes = [vp]
+        L.lmpb_peer_export.argtypes = [vp, C.c_size_t]
+        L.lmpb_peer_import.argtypes = [vp, i32, i32]
+        L.lmpb_peer_close.argtypes = []
+        L.lmpb_peer_size.argtypes = []
+        L.lmpb_reduce_allreduce.argtypes = [i32, i32, vp, P64, i32, i32, vp, vp]
         PI = C.POINTER(C.c_int)
         L.lmpb_gemm_sched_tile.argtypes = [i32, i32, i32, i32, i32, PI, PI]
         L.lmpb_gemm_sched_tile.restype = None
@@ -263,3 +269,36 @@ def allreduce(dtype, ptrs, counts, op=SUM, overlap=False, stream=0) -> None:
 
 def comm_join(stream=0) -> None:
     check(lib().lmpb_comm_join(stream))
+
+
+# ------------------------------------------------- peer-memory collectives
+
+PEER_HANDLE_BYTES = 64
+
+
+def peer_export() -> bytes:
+    buf = C.create_string_buffer(PEER_HANDLE_BYTES)
+    check(lib().lmpb_peer_export(buf, PEER_HANDLE_BYTES))
+    return buf.raw
+
+
+def peer_import(handles: list[bytes], rank: int) -> None:
+    blob = b"".join(handles)
+    buf = C.create_string_buffer(blob, len(blob))
+    check(lib().lmpb_peer_import(buf, len(handles), rank))
+
+
+def peer_close() -> None:
+    check(lib().lmpb_peer_close())
+
+
+def peer_size() -> int:
+    return int(lib().lmpb_peer_size())
+
+
+def reduce_allreduce(op, dt, in_ptr, shape, axis, out_ptr, stream=0) -> int:
+    """lmpb_reduce_allreduce; returns the status (UNSUPPORTED lets the caller fall back)."""
+    st = lib().lmpb_reduce_allreduce(op, dt, in_ptr, shape_arr(shape), len(shape), axis, out_ptr, stream)
+    if st not in (0, 3):
+        check(st)
+    return st

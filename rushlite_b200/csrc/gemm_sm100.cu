@@ -1125,8 +1125,6 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
     const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
     if (vec && !two_pass && Kp <= 4096)
       split_rows_reg_kernel<4><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
-    else if (vec && !two_pass && Kp <= 8192)
-      split_rows_reg_kernel<8><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
     else if (vec)
       split_rows_kernel<true><<<grid, 256, 0, st>>>(src, rows, K, Kp, hi, lo, rowmax, expo);
     else

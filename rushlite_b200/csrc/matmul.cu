@@ -94,9 +94,18 @@ extern "C" lmpb_status lmpb_gemm_f32_bias_act(int trans_a, int trans_b, const fl
   return gemm_f32_sm100(trans_a, trans_b, A, B, C, m, n, k, 0.f, as_stream(stream), bias, clamp, lo, hi);
 }
 
+namespace lmpb {
+unsigned peer_take_error();
+}
+using lmpb::peer_take_error;
+
 extern "C" lmpb_status lmpb_device_error(void) {
   LMPB_CUDA_TRY(cudaDeviceSynchronize());
   const unsigned int e = gemm_take_error();
+  const unsigned int pe = peer_take_error();
+  if (pe != 0)
+    return set_error(LMPB_ERR_TIMEOUT, "fused reduce + all-reduce: a bounded wait for another GPU expired (code " +
+                                           std::to_string(pe) + ")");
   if (e == 0) return LMPB_OK;
   return set_error(LMPB_ERR_TIMEOUT, "tensor-core GEMM: a bounded wait expired (code " + std::to_string(e) + ")");
 }

@@ -29,6 +29,9 @@ namespace lmpb {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kMaxPeerRanks = 8;
+constexpr int64_t kPeerMaxBlocks = 16384;                // column blocks per flag table row
+constexpr long long kPeerWaitCycles = 4000000000ll;      // ~2 s at 1.9 GHz
 
 template <int OP, typename T>
 struct RedOp {
@@ -313,6 +316,135 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Leading-axis reduction fused with the all-reduce of its result across the
+// GPUs of a row-partitioned job, over NVLink peer memory.  Each rank runs the
+// cluster column walk on its own rows; a cluster's rank-0 CTA then pushes its
+// 64-column partial into slot [rank] of every rank's exchange buffer (remote
+// stores), fences, and raises its flag (the call's epoch) in every rank's flag
+// table.  It waits, with a bound, until all ranks' flags for its column block
+// carry the epoch, and folds the partials from its own buffer in rank order,
+// so every rank writes identical results.  Buffers alternate between two
+// halves by epoch parity: a rank reaches epoch e + 2 only after every rank
+// signalled e + 1, i.e. finished reading epoch e.
+struct PeerArgs {
+  unsigned char* data[kMaxPeerRanks];  // each rank's exchange buffer (this process's mapping)
+  unsigned* flags[kMaxPeerRanks];      // each rank's flag table [kMaxPeerRanks][kPeerMaxBlocks]
+  int nranks, rank;
+  unsigned epoch;
+  int64_t slot_bytes;
+};
+
+__device__ unsigned int g_peer_error = 0;
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int OP, typename T, int VW, int CC>
+__global__ void __launch_bounds__(kThreads)
+    reduce_cols_peer_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t R, int64_t inner,
+                            int64_t rows_per_chunk, PeerArgs pa) {
+  namespace cg = cooperative_groups;
+  constexpr int CTX = 16, CTY = kThreads / CTX, DEPTH = 4;
+  using Rd = RedOp<OP, T>;
+  __shared__ T part[CTY][CTX * VW];
+  __shared__ T fin[CTX * VW];
+  const int tx = threadIdx.x % CTX, ty = threadIdx.x / CTX;
+  const int64_t c = ((int64_t)blockIdx.x * CTX + tx) * VW;
+  const int64_t r0 = (int64_t)blockIdx.z * rows_per_chunk;
+  const int64_t r1 = min(R, r0 + rows_per_chunk);
+  T acc[VW];
+#pragma unroll
+  for (int j = 0; j < VW; ++j) acc[j] = Rd::identity();
+  if (c < inner) {
+    const T* base = in + c;
+    int64_t r = r0 + ty;
+    for (; r + (DEPTH - 1) * CTY < r1; r += DEPTH * CTY) {
+      V16<T> x[DEPTH];
+#pragma unroll
+      for (int u = 0; u < DEPTH; ++u) x[u].raw = __ldg(reinterpret_cast<const uint4*>(base + (r + u * CTY) * inner));
+#pragma unroll
+      for (int u = 0; u < DEPTH; ++u)
+#pragma unroll
+        for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x[u].v[j]);
+    }
+    for (; r < r1; r += CTY) {
+      V16<T> x;
+      x.raw = __ldg(reinterpret_cast<const uint4*>(base + r * inner));
+#pragma unroll
+      for (int j = 0; j < VW; ++j) acc[j] = Rd::apply(acc[j], x.v[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VW; ++j) part[ty][tx * VW + j] = acc[j];
+  __syncthreads();
+  if (ty == 0) {
+#pragma unroll
+    for (int j = 0; j < VW; ++j) {
+      T v = part[0][tx * VW + j];
+      for (int k = 1; k < CTY; ++k) v = Rd::apply(v, part[k][tx * VW + j]);
+      fin[tx * VW + j] = v;
+    }
+  }
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  if (cl.block_rank() == 0 && ty == 0) {  // lanes 0..15 of warp 0
+    T v[VW];
+#pragma unroll
+    for (int j = 0; j < VW; ++j) {
+      v[j] = fin[tx * VW + j];
+      for (int k = 1; k < CC; ++k) v[j] = Rd::apply(v[j], cl.map_shared_rank(fin, k)[tx * VW + j]);
+    }
+    const int half = (int)(pa.epoch & 1u);
+    // push this rank's partial into slot [rank] of every rank's buffer
+    if (c < inner)
+      for (int p = 0; p < pa.nranks; ++p) {
+        T* dst = reinterpret_cast<T*>(pa.data[p] + ((int64_t)half * kMaxPeerRanks + pa.rank) * pa.slot_bytes) + c;
+#pragma unroll
+        for (int j = 0; j < VW; ++j) dst[j] = v[j];
+      }
+    __threadfence_system();
+    __syncwarp(0xffffu);
+    bool ok = true;
+    if (tx == 0) {
+      for (int p = 0; p < pa.nranks; ++p)
+        st_release_sys(pa.flags[p] + (int64_t)pa.rank * kPeerMaxBlocks + blockIdx.x, pa.epoch);
+      // wait (bounded) for every rank's partial of this column block
+      const unsigned* mine = pa.flags[pa.rank];
+      const long long t0 = clock64();
+      for (int q = 0; q < pa.nranks && ok; ++q)
+        while (ld_acquire_sys(mine + (int64_t)q * kPeerMaxBlocks + blockIdx.x) - pa.epoch > 0x7fffffffu) {
+          if (clock64() - t0 > kPeerWaitCycles) {
+            atomicExch(&g_peer_error, 1u);
+            ok = false;
+            break;
+          }
+        }
+    }
+    ok = __shfl_sync(0xffffu, ok, 0);
+    if (ok && c < inner) {
+      const unsigned char* mybuf = pa.data[pa.rank];
+#pragma unroll
+      for (int j = 0; j < VW; ++j) {
+        T r = Rd::identity();
+        for (int q = 0; q < pa.nranks; ++q) {
+          const T* src = reinterpret_cast<const T*>(mybuf + ((int64_t)half * kMaxPeerRanks + q) * pa.slot_bytes) + c + j;
+          const T x = *reinterpret_cast<const volatile T*>(src);
+          r = q == 0 ? x : Rd::apply(r, x);
+        }
+        out[c + j] = r;
+      }
+    }
+  }
+  cl.sync();
+}
+
 template <int OP, typename T>
 __global__ void fill_identity_kernel(T* out, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -550,6 +682,88 @@ lmpb_status reduce_with_workspace(int op, int dtype, const void* in, const int64
     return s;
   });
   return set_error(LMPB_ERR_INVALID, "lmpb_reduce: invalid dtype");
+}
+
+// ---------------------------------------------------------------- peer path
+
+size_t peer_region_bytes(int64_t slot_bytes) {
+  return (size_t)2 * kMaxPeerRanks * slot_bytes + (size_t)kMaxPeerRanks * kPeerMaxBlocks * sizeof(unsigned);
+}
+size_t peer_flags_offset(int64_t slot_bytes) { return (size_t)2 * kMaxPeerRanks * slot_bytes; }
+
+unsigned peer_take_error() {
+  unsigned v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_peer_error, sizeof v) != cudaSuccess) return 0xFFFFFFFFu;
+  if (v) cudaMemcpyToSymbol(g_peer_error, &zero, sizeof zero);
+  return v;
+}
+
+// The fused reduce + all-reduce over the ranks' peer-mapped regions `bufs`
+// (each peer_region_bytes(slot_bytes) long: two halves of kMaxPeerRanks data
+// slots, then the flag table).  LMPB_ERR_UNSUPPORTED when this shape does not
+// take the cluster column path, its result does not fit a slot, or its CTAs
+// could not all be resident at once (a rank's waiting CTA must never keep a
+// CTA another rank waits for from running).
+lmpb_status reduce_allreduce_peer(int op, int dtype, const void* in, const int64_t* shape, int ndim, int axis,
+                                  void* out, unsigned char* const* bufs, int nranks, int rank, unsigned epoch,
+                                  int64_t slot_bytes, cudaStream_t st) {
+  LMPB_CHECK_ARG(valid_dtype(dtype), "lmpb_reduce_allreduce: invalid dtype");
+  LMPB_CHECK_ARG(op >= LMPB_SUM && op <= LMPB_PROD, "lmpb_reduce_allreduce: unknown op");
+  LMPB_CHECK_ARG(nranks >= 1 && nranks <= kMaxPeerRanks && rank >= 0 && rank < nranks,
+                 "lmpb_reduce_allreduce: bad rank count");
+  int64_t outer, R, inner;
+  lmpb_status s = reduce_geometry(shape, ndim, axis, outer, R, inner);
+  if (s != LMPB_OK) return s;
+  if (outer != 1 || inner <= 1 || R == 0)
+    return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce_allreduce: only a leading-axis reduction of a matrix");
+  LMPB_CHECK_ARG(in && out, "lmpb_reduce_allreduce: null pointer");
+  LMPB_DISPATCH_DTYPE(dtype, T, {
+    ReducePlan p = plan_reduce<T>(in, out, outer, R, inner);
+    constexpr int N = V16<T>::N;
+    if (!p.cluster || p.S != kClusterChunks || p.vw != N || inner * (int64_t)sizeof(T) > slot_bytes)
+      return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce_allreduce: shape outside the fused path");
+    const int64_t colblocks = (inner / N + 15) / 16;
+    if (colblocks > kPeerMaxBlocks) return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce_allreduce: too many columns");
+    PeerArgs pa{};
+    for (int r = 0; r < nranks; ++r) {
+      pa.data[r] = bufs[r];
+      pa.flags[r] = reinterpret_cast<unsigned*>(bufs[r] + peer_flags_offset(slot_bytes));
+    }
+    pa.nranks = nranks;
+    pa.rank = rank;
+    pa.epoch = epoch;
+    pa.slot_bytes = slot_bytes;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)colblocks, 1, (unsigned)kClusterChunks);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = kClusterChunks;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const int64_t rpc = (R + kClusterChunks - 1) / kClusterChunks;
+    cudaError_t e = cudaSuccess;
+    auto go = [&](auto kern) -> lmpb_status {
+      int active = 0;
+      e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
+      if (e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("cudaOccupancyMaxActiveClusters: ") + cudaGetErrorString(e));
+      if (active < colblocks)
+        return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce_allreduce: the grid does not fit the GPU at once");
+      e = cudaLaunchKernelEx(&cfg, kern, (const T*)in, (T*)out, R, inner, rpc, pa);
+      if (e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("reduce_cols_peer_kernel: ") + cudaGetErrorString(e));
+      return launch_status("reduce_cols_peer_kernel");
+    };
+    switch (op) {
+      case LMPB_SUM: return go(reduce_cols_peer_kernel<LMPB_SUM, T, N, kClusterChunks>);
+      case LMPB_MAX: return go(reduce_cols_peer_kernel<LMPB_MAX, T, N, kClusterChunks>);
+      case LMPB_MIN: return go(reduce_cols_peer_kernel<LMPB_MIN, T, N, kClusterChunks>);
+      default: return go(reduce_cols_peer_kernel<LMPB_PROD, T, N, kClusterChunks>);
+    }
+  });
+  return set_error(LMPB_ERR_INVALID, "lmpb_reduce_allreduce: invalid dtype");
 }
 
 }  // namespace lmpb

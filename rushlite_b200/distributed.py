@@ -62,6 +62,47 @@ def init_comm() -> bool:
     return True
 
 
+def init_peer() -> bool:
+    """Maps every rank's exchange region into this process (CUDA IPC over
+    NVLink; handles exchanged through the torch.distributed group) for the
+    fused leading-axis reduce + all-reduce (reduce_allreduce).  One rank per
+    GPU.  Returns False for one rank."""
+    import torch.distributed as dist
+
+    from . import capi
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return False
+    if capi.peer_size():
+        return True
+    mine = capi.peer_export()
+    handles = [None] * dist.get_world_size()
+    dist.all_gather_object(handles, mine)
+    capi.peer_import(handles, dist.get_rank())
+    dist.barrier()
+    return True
+
+
+def reduce_allreduce(x, op: str = "sum"):
+    """Sum / max / min / prod over axis 0 of a rank's row block of a 2-D
+    Variable, combined over all ranks: the result of the whole row-partitioned
+    tensor, identical on every rank.  With a peer context (init_peer) it is one
+    kernel (lmpb_reduce_allreduce); otherwise, or for a shape outside that
+    kernel, the local reduction followed by all_reduce_."""
+    from . import _C, capi
+
+    fn = {"sum": _C.sum, "max": _C.max, "min": _C.min, "prod": _C.prod}[op]
+    if capi.peer_size() and len(x.shape) == 2:
+        out = _C.zeros([1, x.shape[1]], False, _C.device.cuda, x.dtype)
+        st = capi.reduce_allreduce(capi.REDUCE_OPS[op], int(x.dtype.value), x.data.data_ptr(), list(x.shape), 0,
+                                   out.data.data_ptr(), _stream())
+        if st == 0:
+            return out
+    r = fn(x, 0)
+    all_reduce_(r.data, op)
+    return r
+
+
 def _stream():
     from . import _C
 
