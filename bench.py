@@ -292,6 +292,12 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
     from rushlite_b200 import distributed as D
 
     R, C = 16384, 4096
+    peer = False
+    if world > 1:
+        try:
+            peer = D.init_peer()
+        except Exception as e:  # no peer mapping: the NCCL route
+            print(f"[bench] peer memory unavailable ({e}); dim-0 via NCCL", file=sys.stderr)
     rng = np.random.default_rng(3 + rank)
     xf = rsl.Variable(rng.standard_normal((R, C), dtype=np.float32), requires_grad=True)
     xi = rsl.Variable(rng.integers(-1000, 1001, (R, C)).astype(np.int32), dtype=rsl.dtype.int32)
@@ -303,11 +309,13 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
             out_b = (C if axis == 0 else R) * 4
 
             def run(fn=fn, x=x, axis=axis, name=name):
-                r = fn(x, axis)
                 if axis == 0 and world > 1:
-                    D.all_reduce_(r.data, ops[name])  # the one exchange step
+                    # the one exchange step: reduce + all-reduce in one kernel over
+                    # peer memory (or, without a peer context, the local reduction
+                    # and an NCCL all-reduce)
+                    D.reduce_allreduce(x, ops[name]).realize()
                 else:
-                    r.realize()
+                    fn(x, axis).realize()
 
             ms = D.max_over_ranks(_time(torch, run, args.steps))
             res[f"{name}_dim{axis}"] = {"ms": ms, "GB/s": (nbytes + out_b) / ms / 1e6}
@@ -338,7 +346,10 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
             v["GB/s"] *= world  # aggregate over ranks
     return {"metric": "dim-wise reduction HBM GB/s (C3, all ops)", "value": value, "unit": "GB/s",
             "n_gpus": world, "scaling": "weak",
-            "higher_is_better": True, "dtype": "f32/i32", "config": {"workload": "C3 reductions", "shape": [R, C]},
+            "higher_is_better": True, "dtype": "f32/i32",
+            "config": {"workload": "C3 reductions", "shape": [R, C],
+                       "dim0_exchange": ("one kernel: reduce + all-reduce over NVLink peer memory" if peer
+                                         else ("NCCL all-reduce after the reduction" if world > 1 else "none"))},
             "ops": res, "roofline": {"bound": "hbm", "achieved": value / world, "peak": peak, "unit": "GB/s",
                                      "frac": value / world / peak, "peak_source": src, "per": "GPU"}}
 

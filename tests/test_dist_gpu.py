@@ -112,6 +112,23 @@ def _worker(rank, world, port, q, mode="gloo"):
         for i, (p, p1) in enumerate(zip(P, P1)):
             out[f"dp_grad{i}"] = (p.grad.numpy(), p1.grad.numpy())
         if mode == "lmpb":
+            # the fused reduce + all-reduce over peer memory: one kernel, the
+            # result over all ranks' rows, the same bits on every rank
+            assert D.init_peer()
+            from rushlite_b200 import capi as _capi
+
+            for name, x, op in [("sum", xf, "sum"), ("max", xf, "max"), ("min", xf, "min"), ("isum", xi, "sum")]:
+                dt = rsl.dtype.int32 if x.dtype == np.int32 else rsl.dtype.float32
+                v = rsl.Variable(np.ascontiguousarray(x[r0:r1]), dtype=dt)
+                v.realize()
+                rsl.cuda.synchronize()
+                n0 = _capi.kernel_launches()
+                got = D.reduce_allreduce(v, op)
+                launched = _capi.kernel_launches() - n0
+                fn = {"sum": rsl.sum, "max": rsl.max, "min": rsl.min}[op]
+                out["peer_" + name] = (got.numpy(), fn(rsl.Variable(x, dtype=dt), 0).numpy(), launched)
+            _capi.device_error()
+            _capi.peer_close()
             # overlapped all-reduce on the communication stream, then join
             g = [p.grad for p in P1]
             before = [x.numpy() for x in g]
@@ -166,3 +183,15 @@ def test_two_ranks_on_product_kernels(cuda, mode):
             assert rel_err(g, g1) <= 1e-5, (rank, k, rel_err(g, g1))
         for got, want in out.get("overlap", []):
             assert_bitexact(got, want, f"rank {rank} overlapped all-reduce")
+        for name in ("sum", "max", "min", "isum"):
+            if "peer_" + name not in out:
+                continue
+            got, want, launched = out["peer_" + name]
+            assert launched == 1, (name, launched)  # one fused kernel, no fallback
+            if name == "sum":
+                assert rel_err(got, want) <= 1e-5
+            else:
+                assert_bitexact(got, want, f"rank {rank} peer {name}")
+    if mode == "lmpb":
+        for name in ("sum", "max", "min", "isum"):
+            assert_bitexact(results[0]["peer_" + name][0], results[1]["peer_" + name][0], f"peer {name} across ranks")
