@@ -308,12 +308,15 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
         for axis in (0, 1):
             out_b = (C if axis == 0 else R) * 4
 
-            def run(fn=fn, x=x, axis=axis, name=name):
+            o = rsl.Variable(np.zeros((1, C), np.int32 if name == "int32_sum" else np.float32),
+                             dtype=rsl.dtype.int32 if name == "int32_sum" else rsl.dtype.float32)
+
+            def run(fn=fn, x=x, axis=axis, name=name, o=o):
                 if axis == 0 and world > 1:
                     # the one exchange step: reduce + all-reduce in one kernel over
                     # peer memory (or, without a peer context, the local reduction
                     # and an NCCL all-reduce)
-                    D.reduce_allreduce(x, ops[name]).realize()
+                    D.reduce_allreduce(x, ops[name], out=o).realize()
                 else:
                     fn(x, axis).realize()
 

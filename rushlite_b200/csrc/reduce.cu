@@ -20,6 +20,8 @@
 #include <cooperative_groups.h>
 
 #include <cstdio>
+#include <map>
+#include <mutex>
 #include <cstdlib>
 #include <limits>
 
@@ -747,9 +749,24 @@ lmpb_status reduce_allreduce_peer(int op, int dtype, const void* in, const int64
     const int64_t rpc = (R + kClusterChunks - 1) / kClusterChunks;
     cudaError_t e = cudaSuccess;
     auto go = [&](auto kern) -> lmpb_status {
+      // clusters that fit the GPU at once, per device and kernel (the query is slow)
+      static std::mutex mu;
+      static std::map<std::pair<int, const void*>, int> fits;
+      int dev = 0;
+      cudaGetDevice(&dev);
       int active = 0;
-      e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
-      if (e != cudaSuccess) return set_error(LMPB_ERR_CUDA, std::string("cudaOccupancyMaxActiveClusters: ") + cudaGetErrorString(e));
+      {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = fits.find({dev, (const void*)kern});
+        if (it != fits.end()) {
+          active = it->second;
+        } else {
+          e = cudaOccupancyMaxActiveClusters(&active, kern, &cfg);
+          if (e != cudaSuccess)
+            return set_error(LMPB_ERR_CUDA, std::string("cudaOccupancyMaxActiveClusters: ") + cudaGetErrorString(e));
+          fits[{dev, (const void*)kern}] = active;
+        }
+      }
       if (active < colblocks)
         return set_error(LMPB_ERR_UNSUPPORTED, "lmpb_reduce_allreduce: the grid does not fit the GPU at once");
       e = cudaLaunchKernelEx(&cfg, kern, (const T*)in, (T*)out, R, inner, rpc, pa);

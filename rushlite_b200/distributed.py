@@ -71,8 +71,8 @@ def init_peer() -> bool:
 
     from . import capi
 
-    if not dist.is_initialized() or dist.get_world_size() == 1:
-        return False
+    if not dist.is_initialized() or dist.get_world_size() == 1 or os.environ.get("LMPB_PEER") == "0":
+        return False  # LMPB_PEER=0: A/B switch, keep the NCCL route
     if capi.peer_size():
         return True
     mine = capi.peer_export()
@@ -83,17 +83,19 @@ def init_peer() -> bool:
     return True
 
 
-def reduce_allreduce(x, op: str = "sum"):
+def reduce_allreduce(x, op: str = "sum", out=None):
     """Sum / max / min / prod over axis 0 of a rank's row block of a 2-D
     Variable, combined over all ranks: the result of the whole row-partitioned
     tensor, identical on every rank.  With a peer context (init_peer) it is one
-    kernel (lmpb_reduce_allreduce); otherwise, or for a shape outside that
-    kernel, the local reduction followed by all_reduce_."""
+    kernel (lmpb_reduce_allreduce), written into `out` when given; otherwise,
+    or for a shape outside that kernel, the local reduction followed by
+    all_reduce_."""
     from . import _C, capi
 
     fn = {"sum": _C.sum, "max": _C.max, "min": _C.min, "prod": _C.prod}[op]
     if capi.peer_size() and len(x.shape) == 2:
-        out = _C.zeros([1, x.shape[1]], False, _C.device.cuda, x.dtype)
+        if out is None:  # `out`: a [1, cols] Variable of x's dtype to write into
+            out = _C.zeros([1, x.shape[1]], False, _C.device.cuda, x.dtype)
         st = capi.reduce_allreduce(capi.REDUCE_OPS[op], int(x.dtype.value), x.data.data_ptr(), list(x.shape), 0,
                                    out.data.data_ptr(), _stream())
         if st == 0:

@@ -120,10 +120,12 @@ def _worker(rank, world, port, q, mode="gloo"):
             for name, x, op in [("sum", xf, "sum"), ("max", xf, "max"), ("min", xf, "min"), ("isum", xi, "sum")]:
                 dt = rsl.dtype.int32 if x.dtype == np.int32 else rsl.dtype.float32
                 v = rsl.Variable(np.ascontiguousarray(x[r0:r1]), dtype=dt)
+                o = rsl.Variable(np.zeros((1, x.shape[1]), x.dtype), dtype=dt)
                 v.realize()
+                o.realize()
                 rsl.cuda.synchronize()
                 n0 = _capi.kernel_launches()
-                got = D.reduce_allreduce(v, op)
+                got = D.reduce_allreduce(v, op, out=o)
                 launched = _capi.kernel_launches() - n0
                 fn = {"sum": rsl.sum, "max": rsl.max, "min": rsl.min}[op]
                 out["peer_" + name] = (got.numpy(), fn(rsl.Variable(x, dtype=dt), 0).numpy(), launched)
