@@ -264,7 +264,7 @@ def _backlog(torch, ms=20.0):
     torch.cuda._sleep(int(ms * 1e-3 * 1.9e9))
 
 
-def _time(torch, fn, iters, warmup=3):
+def _time(torch, fn, iters, warmup=3, backlog_ms=20.0):
     """Median device time of one call of fn (ms): an event after every call,
     launches queued behind a sleep kernel.  The median keeps a host hiccup
     (these hosts are shared) from showing up as device time; the mean is
@@ -273,7 +273,7 @@ def _time(torch, fn, iters, warmup=3):
         fn()
     torch.cuda.synchronize()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
-    _backlog(torch)
+    _backlog(torch, backlog_ms)
     evs[0].record()
     for i in range(iters):
         fn()
@@ -320,7 +320,9 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
                 else:
                     fn(x, axis).realize()
 
-            ms = D.max_over_ranks(_time(torch, run, args.steps))
+            # a collective per call: a longer backlog keeps every call queued
+            # before the first runs, so the times are device time, not the host's
+            ms = D.max_over_ranks(_time(torch, run, args.steps, backlog_ms=200.0 if world > 1 else 20.0))
             res[f"{name}_dim{axis}"] = {"ms": ms, "GB/s": (nbytes + out_b) / ms / 1e6}
             tot_b += nbytes + out_b
             tot_ms += ms
