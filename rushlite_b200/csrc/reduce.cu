@@ -339,14 +339,6 @@ struct PeerArgs {
 
 __device__ unsigned int g_peer_error = 0;
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 template <int OP, typename T, int VW, int CC>
 __global__ void __launch_bounds__(kThreads)
@@ -405,29 +397,34 @@ __global__ void __launch_bounds__(kThreads)
     }
     const int half = (int)(pa.epoch & 1u);
     // push this rank's partial into slot [rank] of every rank's buffer
-    if (c < inner)
+    if (c < inner) {  // one 16-byte store per rank (VW * sizeof(T) == 16 on this path)
+      V16<T> pk;
+#pragma unroll
+      for (int j = 0; j < VW; ++j) pk.v[j] = v[j];
       for (int p = 0; p < pa.nranks; ++p) {
         T* dst = reinterpret_cast<T*>(pa.data[p] + ((int64_t)half * kMaxPeerRanks + pa.rank) * pa.slot_bytes) + c;
-#pragma unroll
-        for (int j = 0; j < VW; ++j) dst[j] = v[j];
+        *reinterpret_cast<uint4*>(dst) = pk.raw;
       }
-    __threadfence_system();
+    }
+    __threadfence_system();  // the partials are visible everywhere before any flag
     __syncwarp(0xffffu);
     bool ok = true;
     if (tx == 0) {
       for (int p = 0; p < pa.nranks; ++p)
-        st_release_sys(pa.flags[p] + (int64_t)pa.rank * kPeerMaxBlocks + blockIdx.x, pa.epoch);
-      // wait (bounded) for every rank's partial of this column block
-      const unsigned* mine = pa.flags[pa.rank];
+        *reinterpret_cast<volatile unsigned*>(pa.flags[p] + (int64_t)pa.rank * kPeerMaxBlocks + blockIdx.x) = pa.epoch;
+      // wait (bounded) for every rank's partial of this column block: relaxed
+      // polling, one system-scope fence once all flags are seen
+      const volatile unsigned* mine = pa.flags[pa.rank];
       const long long t0 = clock64();
       for (int q = 0; q < pa.nranks && ok; ++q)
-        while (ld_acquire_sys(mine + (int64_t)q * kPeerMaxBlocks + blockIdx.x) - pa.epoch > 0x7fffffffu) {
+        while (mine[(int64_t)q * kPeerMaxBlocks + blockIdx.x] - pa.epoch > 0x7fffffffu) {
           if (clock64() - t0 > kPeerWaitCycles) {
             atomicExch(&g_peer_error, 1u);
             ok = false;
             break;
           }
         }
+      __threadfence_system();
     }
     ok = __shfl_sync(0xffffu, ok, 0);
     if (ok && c < inner) {
