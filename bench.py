@@ -301,6 +301,21 @@ def workload_c3(rsl, torch, args, rank=0, world=1):
     rng = np.random.default_rng(3 + rank)
     xf = rsl.Variable(rng.standard_normal((R, C), dtype=np.float32), requires_grad=True)
     xi = rsl.Variable(rng.integers(-1000, 1001, (R, C)).astype(np.int32), dtype=rsl.dtype.int32)
+    if peer:
+        # one checked call first: if a rank's bounded wait for the others ever
+        # expires, every rank drops to the NCCL route instead of timing out per call
+        from rushlite_b200 import capi
+
+        D.reduce_allreduce(xf, "sum").realize()
+        try:
+            capi.device_error()
+            ok = 1.0
+        except capi.LmpbError as e:
+            print(f"[bench] fused reduce + all-reduce failed ({e}); dim-0 via NCCL", file=sys.stderr)
+            ok = 0.0
+        if D.max_over_ranks(-ok) != -1.0:  # any rank failed
+            capi.peer_close()
+            peer = False
     nbytes = R * C * 4
     res, tot_b, tot_ms = {}, 0, 0.0
     ops = {"sum": "sum", "max": "max", "min": "min", "int32_sum": "sum"}
