@@ -72,6 +72,10 @@ Variable record(const Tensor& result, variable_list inputs, B backward) {
 // still the untouched zero; other dtypes take the reference's
 // matmul-then-accumulate route.
 void gemm_accumulate(Variable& v, const Tensor& A, bool ta, const Tensor& B, bool tb) {
+  if (v.impl()->grad_shared) {  // the GEMM accumulates in place: give v a gradient of its own first
+    v.impl()->grad_shared = false;
+    v.grad_slot() = tops::add(v.grad_slot(), tensor::zeros_like(v.grad_slot()));
+  }
   Tensor& G = v.grad_slot();
   const bool fp32 = A.type() == DataType::Float32 && B.type() == DataType::Float32 &&
                     G.type() == DataType::Float32 && G.device() == DeviceType::CUDA;
@@ -130,6 +134,7 @@ const Tensor& Variable::grad() const {
 
 void Variable::zero_grad() {
   LMP_CHECK(requires_grad(), "Cannot access grad() if requires_grad = false");
+  impl_->grad_shared = false;
   impl_->grad = tensor::zeros_like(impl_->grad);
   impl_->grad_fn = nullptr;
 }
@@ -146,6 +151,29 @@ void Variable::incr_grad(const Tensor& g) {
     return;
   }
   const ImplPtr& gi = G.impl();
+  if (impl_->grad_fn && !impl_->grad_shared && gi->lazy && gi->lazy->kind == LazyNode::kConst &&
+      gi->lazy->p0 == 0.0 && !gi->storage && g.type() == G.type() && g.defined()) {
+    // An intermediate's first gradient term: keep g itself rather than 0 + g,
+    // so the kernel that materialises g (for a GEMM operand, say) also serves
+    // every other reader of this gradient (the bias gradient's row sum).
+    G = g;
+    impl_->grad_shared = true;
+    return;
+  }
+  if (impl_->grad_shared) {  // copy on write: a new pending sum, the shared tensor untouched
+    auto n = std::make_shared<LazyNode>();
+    n->kind = LazyNode::kBinary;
+    n->op = LMPB_ADD;
+    n->inputs = {gi, g.impl()};
+    auto t = std::make_shared<TensorImpl>();
+    t->shape = gi->shape;
+    t->dtype = gi->dtype;
+    t->device = gi->device;
+    t->lazy = n;
+    G = Tensor(t);
+    impl_->grad_shared = false;
+    return;
+  }
   auto old = std::make_shared<TensorImpl>();
   old->shape = gi->shape;
   old->dtype = gi->dtype;
@@ -196,6 +224,16 @@ void Variable::backward() {
     if (gi->lazy && gi->lazy->kind != LazyNode::kConst) stale.push_back(gi);
   }
   if (!stale.empty()) tensor::realize_all(stale);
+  // A gradient shared with another tensor (an intermediate's first term, kept
+  // as is) gets a private copy now, before this sweep updates either in place.
+  std::vector<ImplPtr> copies;
+  for (Variable& node : topo) {
+    if (!node.impl()->grad_shared) continue;
+    node.impl()->grad_shared = false;
+    node.grad_slot() = tops::add(node.grad_slot(), tensor::zeros_like(node.grad_slot()));
+    copies.push_back(node.grad_slot().impl());
+  }
+  if (!copies.empty()) tensor::realize_all(copies);
   impl_->grad = tensor::ones_like(impl_->grad);
   {
     tensor::lazy::CaptureGuard cap(true);

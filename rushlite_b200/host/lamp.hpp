@@ -307,6 +307,11 @@ struct VariableImpl {
   // the backend stream; lets a data-parallel caller start that gradient's
   // all-reduce while the rest of the backward is still running.
   std::function<void()> grad_hook;
+  // The gradient is the very tensor another gradient expression produced (an
+  // intermediate's first contribution is taken as is, not as 0 + g), so
+  // realizing either materialises both; it must be copied before it is
+  // updated in place.
+  bool grad_shared = false;
 };
 
 class Variable {
