@@ -13,6 +13,15 @@ Multi-GPU (torchrun, one process per GPU): the chain is partitioned along the
 leading dim; each rank owns an [8192, 8192] row block of a [8192*N, 8192]
 problem (weak scaling).  No data-path collective: rows are independent.
 
+The same JSON line carries a "secondary" block for each other BASELINE
+config, with its own clock record, roofline and (at N = 1) CPU baseline:
+C3 reductions (GB/s), C4 matmul sweep (TFLOP/s), C5 data-parallel MLP
+(steps/s; the step recorded once as a CUDA graph and replayed), C1 README MLP
+(steps/s) and the C2 ops issued eagerly (GB/s).  Under torchrun the blocks
+are C3 (its dim-0 partials combined across ranks) and C5 (strong scaling,
+gradient all-reduce overlapped with the backward).  --no-secondary skips them;
+--workload runs one of them alone.
+
 --impl reference runs the reference's own CPU implementation (its CPU core,
 compiled from its sources into oracle/_ref) on the host cores instead.
 """
