@@ -88,7 +88,8 @@ constexpr int P_STAGES = 6;
 constexpr int P_A_TILE = 128 * BK * 2;                       // 8 KB
 constexpr int P_B_TILE = 128 * BK * 2;                       // 8 KB: half of N
 constexpr int P_STAGE_BYTES = 2 * P_A_TILE + 2 * P_B_TILE;  // 32 KB per CTA
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_EPI_BYTES = 8 * 32 * 32 * 4;  // per epilogue warp a 32 x 32 fp32 staging block
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256 + P_EPI_BYTES;
 constexpr int P_TM = 256;  // output tile rows per pair
 constexpr int kThreadsP = 320;  // producer, MMA, 8 epilogue warps
 
@@ -226,10 +227,24 @@ __host__ __device__ __forceinline__ int row_exp(float mx) {
   return 15 - p;
 }
 
-// x * 2^e, exact (up to one rounding when the result is subnormal).
+// x * 2^e, exact unless the result is subnormal.  Row exponents lie in
+// [-114, 163], so the epilogue's e = -(e_row + e_col) stays within +-330:
+// outside one power of two's range, three steps of at most 2^+-126 each.
+// The steps share e's sign, so every intermediate lies between x and the
+// result, and only a subnormal result can be rounded (possibly twice).  The
+// steps are plain multiplies: the epilogue inlines this 128 times per
+// thread, and a library call there bloats the kernel past the instruction
+// cache (measured on B200, the 1024 x 4096 x 4096 product with its split
+// pass: 182 us with ldexpf in the rare branch, 146 us without).
 __device__ __forceinline__ float pow2_scale(float x, int e) {
   if (e >= -126 && e <= 127) return x * __int_as_float((e + 127) << 23);
-  return ldexpf(x, e);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int s = max(-126, min(126, e));
+    x *= __int_as_float((s + 127) << 23);
+    e -= s;
+  }
+  return x;
 }
 
 // Scaled element -> (hi, lo): hi = fp16(xs), lo = fp16((xs - hi) * 2^11).
@@ -863,6 +878,7 @@ __global__ void __launch_bounds__(kThreadsP, 1)
   uint64_t* tfull = empty + P_STAGES;
   uint64_t* tempty = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
+  float4* epi_stage = reinterpret_cast<float4*>(smem + P_STAGES * P_STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -1031,13 +1047,59 @@ __global__ void __launch_bounds__(kThreadsP, 1)
             store_quad(crow + c, c0 + c, N, vec, erow, eB, a, beta, ep);
           }
         }
-      } else if (ok && row < M) {
-        const int erow = __ldg(eA + row);
+      } else if (ok) {
+        // Each thread holds one row: unscale 32 columns at a time into the
+        // warp's staging block (float4 j of row r at slot j ^ (r & 7), so
+        // neither side conflicts on banks), then write them out row-wise,
+        // 8 lanes per 128-byte row segment, so every store is coalesced.
         const int c0 = n0 + h * 128;
-        float* crow = C + (int64_t)row * N + c0;
+        const int wrow0 = m0 + (int)rank * 128 + q * 32;
+        const int erow = row < M ? __ldg(eA + row) : 0;
+        float4* sw = epi_stage + (warp - 2) * 256;
 #pragma unroll
-        for (int c = 0; c < 128; c += 4)
-          store_quad(crow + c, c0 + c, N, vec, erow, eB, make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]), beta, ep);
+        for (int cc = 0; cc < 128; cc += 32) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int col = c0 + cc + 4 * j;
+            // eB holds n exponents in a buffer padded to 64: the lanes past n
+            // read padding, and their columns are never stored
+            const int4 ec = col < N ? __ldg(reinterpret_cast<const int4*>(eB + col)) : make_int4(0, 0, 0, 0);
+            const float* x = v + cc + 4 * j;
+            sw[lane * 8 + (j ^ (lane & 7))] =
+                make_float4(pow2_scale(x[0], -(erow + ec.x)), pow2_scale(x[1], -(erow + ec.y)),
+                            pow2_scale(x[2], -(erow + ec.z)), pow2_scale(x[3], -(erow + ec.w)));
+          }
+          __syncwarp();
+          const int j = lane & 7, col = c0 + cc + 4 * j;
+#pragma unroll 1
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3), grow = wrow0 + r;
+            float4 o = sw[r * 8 + (j ^ (r & 7))];
+            if (grow < M && col < N && !vec) {  // a row pitch not a multiple of 16 bytes
+              float* dst = C + (int64_t)grow * N + col;
+              const float ov[4] = {o.x, o.y, o.z, o.w};
+              for (int e = 0; e < 4 && col + e < N; ++e)
+                dst[e] = epilogue_apply(ep, beta ? __fadd_rn(dst[e], ov[e]) : ov[e], col + e);
+            } else if (grow < M && col < N) {
+              float4* dst = reinterpret_cast<float4*>(C + (int64_t)grow * N + col);
+              if (beta) {
+                const float4 p = *dst;
+                o.x = __fadd_rn(p.x, o.x);
+                o.y = __fadd_rn(p.y, o.y);
+                o.z = __fadd_rn(p.z, o.z);
+                o.w = __fadd_rn(p.w, o.w);
+              }
+              if (ep.bias || ep.clamp) {
+                o.x = epilogue_apply(ep, o.x, col);
+                o.y = epilogue_apply(ep, o.y, col + 1);
+                o.z = epilogue_apply(ep, o.z, col + 2);
+                o.w = epilogue_apply(ep, o.w, col + 3);
+              }
+              *dst = o;
+            }
+          }
+          __syncwarp();
+        }
       }
       (void)ks;
       if (!ok) break;
