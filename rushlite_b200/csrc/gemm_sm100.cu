@@ -383,15 +383,14 @@ __global__ void __launch_bounds__(256)
 }
 
 // colmax_kernel with 16-byte loads (rows % 4 == 0, src 16-byte aligned): a
-// CTA is 16 column quads (64 columns) x 16 k-lanes over 512 k, each thread
+// CTA is 16 column quads (64 columns) x 16 k-lanes over one k chunk (a multiple of 64), each thread
 // with 4 loads in flight.  Max is order-free, so the maxima are the same.
-constexpr int kColmaxK = 512;
 __global__ void __launch_bounds__(256)
-    colmax4_kernel(const float* __restrict__ src, int64_t rows, int64_t K, unsigned* __restrict__ colmax) {
+    colmax4_kernel(const float* __restrict__ src, int64_t rows, int64_t K, int kchunk, unsigned* __restrict__ colmax) {
   __shared__ float4 part[16][16];
   const int tq = threadIdx.x & 15, tk = threadIdx.x >> 4;
   const int64_t r = (int64_t)blockIdx.x * 64 + 4 * tq;
-  const int64_t k0 = (int64_t)blockIdx.y * kColmaxK, k1 = k0 + kColmaxK < K ? k0 + kColmaxK : K;
+  const int64_t k0 = (int64_t)blockIdx.y * kchunk, k1 = k0 + kchunk < K ? k0 + kchunk : K;
   float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
   if (r < rows) {
     const float* base = src + r;
@@ -829,16 +828,40 @@ __host__ __device__ constexpr uint32_t instr_desc_pair() {
   return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(P_TM >> 4) << 24);
 }
 
-// Four adjacent outputs of one row (columns col..col+3 at dst): unscale by
-// 2^-(e_row+e_col), + C when beta, then the epilogue's bias and clamp.
-__device__ __forceinline__ void store_quad(float* dst, int col, int N, bool vec, int erow, const int* __restrict__ eB,
-                                           float4 v, int beta, const Epilogue& ep) {
-  if (vec && col + 3 < N) {
-    const int4 ec = __ldg(reinterpret_cast<const int4*>(eB + col));
-    float4 o = make_float4(pow2_scale(v.x, -(erow + ec.x)), pow2_scale(v.y, -(erow + ec.y)),
-                           pow2_scale(v.z, -(erow + ec.z)), pow2_scale(v.w, -(erow + ec.w)));
+// The pair kernel's epilogue writes each warp's 32 rows 32 columns at a
+// time through a 32 x 32 fp32 staging block in shared memory: every lane
+// parks four unscaled values of its own row (float4 j of row r at slot
+// j ^ (r & 7), so neither side conflicts on banks), then the warp writes the
+// block out row-wise, 8 lanes per 128-byte row segment, so every store is
+// coalesced.  eB holds n exponents in a buffer padded to 64: lanes past n
+// read padding, and their columns are never stored.
+__device__ __forceinline__ void stage_quad(float4* sw, int lane, int j, float4 v, int erow, const int* __restrict__ eB,
+                                           int col, int N) {
+  const int4 ec = col < N ? __ldg(reinterpret_cast<const int4*>(eB + col)) : make_int4(0, 0, 0, 0);
+  sw[lane * 8 + (j ^ (lane & 7))] = make_float4(pow2_scale(v.x, -(erow + ec.x)), pow2_scale(v.y, -(erow + ec.y)),
+                                                pow2_scale(v.z, -(erow + ec.z)), pow2_scale(v.w, -(erow + ec.w)));
+}
+
+// Rows wrow0 .. wrow0 + 31, columns col0 .. col0 + 31 of C from the staging
+// block: + C when beta, then the bias and clamp epilogue.
+__device__ __forceinline__ void flush_block(const float4* sw, int lane, int wrow0, int col0, int M, int N, bool vec,
+                                            int beta, const Epilogue& ep, float* __restrict__ C) {
+  const int j = lane & 7, col = col0 + 4 * j;
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3), grow = wrow0 + r;
+    float4 o = sw[r * 8 + (j ^ (r & 7))];
+    if (grow >= M || col >= N) continue;
+    if (!vec) {  // a row pitch that is not a multiple of 16 bytes
+      float* dst = C + (int64_t)grow * N + col;
+      const float ov[4] = {o.x, o.y, o.z, o.w};
+      for (int e = 0; e < 4 && col + e < N; ++e)
+        dst[e] = epilogue_apply(ep, beta ? __fadd_rn(dst[e], ov[e]) : ov[e], col + e);
+      continue;
+    }
+    float4* dst = reinterpret_cast<float4*>(C + (int64_t)grow * N + col);
     if (beta) {
-      const float4 p = *reinterpret_cast<const float4*>(dst);
+      const float4 p = *dst;
       o.x = __fadd_rn(p.x, o.x);
       o.y = __fadd_rn(p.y, o.y);
       o.z = __fadd_rn(p.z, o.z);
@@ -850,16 +873,7 @@ __device__ __forceinline__ void store_quad(float* dst, int col, int N, bool vec,
       o.z = epilogue_apply(ep, o.z, col + 2);
       o.w = epilogue_apply(ep, o.w, col + 3);
     }
-    *reinterpret_cast<float4*>(dst) = o;
-  } else {
-    const float vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (col + i < N) {
-        float o = pow2_scale(vv[i], -(erow + __ldg(eB + col + i)));
-        if (beta) o = __fadd_rn(dst[i], o);
-        dst[i] = epilogue_apply(ep, o, col + i);
-      }
+    *dst = o;
   }
 }
 
@@ -1028,30 +1042,34 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         unsigned prev = 0;
         if (lane == 0) prev = atomicAdd(arrivals + (size_t)t * 16 + blk, 1u);
         prev = __shfl_sync(0xffffffffu, prev, 0);
-        if (prev == (unsigned)(splits - 1) && ok && row < M) {
+        if (prev == (unsigned)(splits - 1) && ok) {
           __threadfence();
-          const int erow = __ldg(eA + row);
+          const int erow = row < M ? __ldg(eA + row) : 0;
           const int c0 = n0 + h * 128;
-          float* crow = C + (int64_t)row * N + c0;
+          const int wrow0 = m0 + (int)rank * 128 + q * 32;
+          float4* sw = epi_stage + (warp - 2) * 256;
           const float4* tp = reinterpret_cast<const float4*>(part + ((size_t)t * splits * 16 + blk) * bsz);
-#pragma unroll 4
-          for (int c = 0; c < 128; c += 4) {
-            float4 a = __ldcg(tp + (c >> 2) * 32 + lane);
-            for (int k = 1; k < splits; ++k) {
-              const float4 b = __ldcg(tp + (size_t)k * 16 * (bsz / 4) + (c >> 2) * 32 + lane);
-              a.x = __fadd_rn(a.x, b.x);
-              a.y = __fadd_rn(a.y, b.y);
-              a.z = __fadd_rn(a.z, b.z);
-              a.w = __fadd_rn(a.w, b.w);
+#pragma unroll 1
+          for (int cc = 0; cc < 128; cc += 32) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int at = ((cc >> 2) + j) * 32 + lane;
+              float4 a = __ldcg(tp + at);
+              for (int k = 1; k < splits; ++k) {
+                const float4 b = __ldcg(tp + (size_t)k * 16 * (bsz / 4) + at);
+                a.x = __fadd_rn(a.x, b.x);
+                a.y = __fadd_rn(a.y, b.y);
+                a.z = __fadd_rn(a.z, b.z);
+                a.w = __fadd_rn(a.w, b.w);
+              }
+              stage_quad(sw, lane, j, a, erow, eB, c0 + cc + 4 * j, N);
             }
-            store_quad(crow + c, c0 + c, N, vec, erow, eB, a, beta, ep);
+            __syncwarp();
+            flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, C);
+            __syncwarp();
           }
         }
       } else if (ok) {
-        // Each thread holds one row: unscale 32 columns at a time into the
-        // warp's staging block (float4 j of row r at slot j ^ (r & 7), so
-        // neither side conflicts on banks), then write them out row-wise,
-        // 8 lanes per 128-byte row segment, so every store is coalesced.
         const int c0 = n0 + h * 128;
         const int wrow0 = m0 + (int)rank * 128 + q * 32;
         const int erow = row < M ? __ldg(eA + row) : 0;
@@ -1059,45 +1077,11 @@ __global__ void __launch_bounds__(kThreadsP, 1)
 #pragma unroll
         for (int cc = 0; cc < 128; cc += 32) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = c0 + cc + 4 * j;
-            // eB holds n exponents in a buffer padded to 64: the lanes past n
-            // read padding, and their columns are never stored
-            const int4 ec = col < N ? __ldg(reinterpret_cast<const int4*>(eB + col)) : make_int4(0, 0, 0, 0);
-            const float* x = v + cc + 4 * j;
-            sw[lane * 8 + (j ^ (lane & 7))] =
-                make_float4(pow2_scale(x[0], -(erow + ec.x)), pow2_scale(x[1], -(erow + ec.y)),
-                            pow2_scale(x[2], -(erow + ec.z)), pow2_scale(x[3], -(erow + ec.w)));
-          }
+          for (int j = 0; j < 8; ++j)
+            stage_quad(sw, lane, j, make_float4(v[cc + 4 * j], v[cc + 4 * j + 1], v[cc + 4 * j + 2], v[cc + 4 * j + 3]),
+                       erow, eB, c0 + cc + 4 * j, N);
           __syncwarp();
-          const int j = lane & 7, col = c0 + cc + 4 * j;
-#pragma unroll 1
-          for (int i = 0; i < 8; ++i) {
-            const int r = i * 4 + (lane >> 3), grow = wrow0 + r;
-            float4 o = sw[r * 8 + (j ^ (r & 7))];
-            if (grow < M && col < N && !vec) {  // a row pitch not a multiple of 16 bytes
-              float* dst = C + (int64_t)grow * N + col;
-              const float ov[4] = {o.x, o.y, o.z, o.w};
-              for (int e = 0; e < 4 && col + e < N; ++e)
-                dst[e] = epilogue_apply(ep, beta ? __fadd_rn(dst[e], ov[e]) : ov[e], col + e);
-            } else if (grow < M && col < N) {
-              float4* dst = reinterpret_cast<float4*>(C + (int64_t)grow * N + col);
-              if (beta) {
-                const float4 p = *dst;
-                o.x = __fadd_rn(p.x, o.x);
-                o.y = __fadd_rn(p.y, o.y);
-                o.z = __fadd_rn(p.z, o.z);
-                o.w = __fadd_rn(p.w, o.w);
-              }
-              if (ep.bias || ep.clamp) {
-                o.x = epilogue_apply(ep, o.x, col);
-                o.y = epilogue_apply(ep, o.y, col + 1);
-                o.z = epilogue_apply(ep, o.z, col + 2);
-                o.w = epilogue_apply(ep, o.w, col + 3);
-              }
-              *dst = o;
-            }
-          }
+          flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, C);
           __syncwarp();
         }
       }
@@ -1197,9 +1181,15 @@ lmpb_status split_operand(const float* src, bool kmajor, int64_t rows, int64_t K
     return set_error(LMPB_ERR_UNSUPPORTED, "gemm: K too large for the split pass");
   const bool quad = (rows & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
   static const bool scalar_colmax = getenv("LMPB_GEMM_COLMAX1") != nullptr;  // A/B switch
-  if (quad && !scalar_colmax)
-    colmax4_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + kColmaxK - 1) / kColmaxK)), 256, 0, st>>>(
-        src, rows, K, reinterpret_cast<unsigned*>(rowmax));
+  if (quad && !scalar_colmax) {
+    // k chunks (multiples of 64) sized so that the grid holds about 8 CTAs
+    // per SM: a [1024, 4096] operand is 64 column blocks, 16 chunks of 64
+    const int64_t gx = (rows + 63) / 64;
+    const int64_t ky = std::max<int64_t>(1, ((int64_t)sm_count() * 8 + gx - 1) / gx);
+    const int64_t kchunk = std::max<int64_t>(64, ((K + ky - 1) / ky + 63) / 64 * 64);
+    colmax4_kernel<<<dim3((unsigned)gx, (unsigned)((K + kchunk - 1) / kchunk)), 256, 0, st>>>(
+        src, rows, K, (int)kchunk, reinterpret_cast<unsigned*>(rowmax));
+  }
   else
     colmax_kernel<<<dim3((unsigned)((rows + 63) / 64), (unsigned)((K + 255) / 256)), 256, 0, st>>>(
         src, rows, K, reinterpret_cast<unsigned*>(rowmax));
