@@ -422,7 +422,10 @@ def workload_c2eager(rsl, torch, args):
 def workload_c4(rsl, torch, args):
     """fp32 matmul sweep through the public API, forward and dA/dB (3 GEMMs, 6MNK flops)."""
     out, tot_f, tot_ms = {}, 0.0, 0.0
-    for (m, k, n) in [(1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (32768, 4096, 4096)]:
+    shapes = [(1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (32768, 4096, 4096)]
+    if args.shape:  # one shape, for profiling (not the C4 config)
+        shapes = [tuple(int(v) for v in args.shape.split(","))]
+    for (m, k, n) in shapes:
         rng = np.random.default_rng(m + k + n)
         A = rsl.Variable((rng.standard_normal((m, k)) / np.sqrt(k)).astype(np.float32), requires_grad=True)
         B = rsl.Variable((rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32), requires_grad=True)
@@ -444,7 +447,8 @@ def workload_c4(rsl, torch, args):
     return {"metric": "fp32 matmul TFLOP/s, fwd + dA + dB (C4 sweep)", "value": value, "unit": "TFLOP/s",
             "timing": "median of per-call CUDA-event times per shape (mean beside it)",
             "higher_is_better": True, "dtype": "f32 (scaled fp16 hi/lo split, 3 MMAs, on tcgen05)",
-            "config": {"workload": "C4 matmul sweep"}, "shapes": out,
+            "config": {"workload": "C4 matmul sweep" if not args.shape else f"one matmul {args.shape} (M,K,N)"},
+            "shapes": out,
             "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s",
                          "frac": value / peak,
                          "peak_source": "measured bf16 GEMM / 3 (three fp16 MMAs per fp32 product)",
@@ -876,6 +880,7 @@ def main():
                     help="headline (C2) only; by default the line also carries C3, C4, C5 and C1 blocks")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--batch", type=int, default=8192, help="C5 global batch (8192 = the config)")
+    ap.add_argument("--shape", default=None, help="C4: one matmul M,K,N instead of the sweep (for profiling)")
     ap.add_argument("--rows", type=int, default=8192, help="rows of a (8192 = the C2 config; smaller for profiling)")
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c2eager"],
                     help="c2 (default) is the headline; the others are the secondary BASELINE configs")
