@@ -830,28 +830,33 @@ __host__ __device__ constexpr uint32_t instr_desc_pair() {
 
 // The pair kernel's epilogue writes each warp's 32 rows 32 columns at a
 // time through a 32 x 32 fp32 staging block in shared memory: every lane
-// parks four unscaled values of its own row (float4 j of row r at slot
-// j ^ (r & 7), so neither side conflicts on banks), then the warp writes the
-// block out row-wise, 8 lanes per 128-byte row segment, so every store is
-// coalesced.  eB holds n exponents in a buffer padded to 64: lanes past n
-// read padding, and their columns are never stored.
-__device__ __forceinline__ void stage_quad(float4* sw, int lane, int j, float4 v, int erow, const int* __restrict__ eB,
-                                           int col, int N) {
-  const int4 ec = col < N ? __ldg(reinterpret_cast<const int4*>(eB + col)) : make_int4(0, 0, 0, 0);
-  sw[lane * 8 + (j ^ (lane & 7))] = make_float4(pow2_scale(v.x, -(erow + ec.x)), pow2_scale(v.y, -(erow + ec.y)),
-                                                pow2_scale(v.z, -(erow + ec.z)), pow2_scale(v.w, -(erow + ec.w)));
+// parks four scaled sums of its own row (float4 j of row r at slot
+// j ^ (r & 7), so neither side conflicts on banks), then the warp unscales
+// and writes the block out row-wise, 8 lanes per 128-byte row segment, so
+// every store is coalesced.  The unscale sits in the write-out loop, which
+// is not unrolled: the code exists once, not once per value held.
+__device__ __forceinline__ void stage_quad(float4* sw, int lane, int j, float4 v) {
+  sw[lane * 8 + (j ^ (lane & 7))] = v;
 }
 
 // Rows wrow0 .. wrow0 + 31, columns col0 .. col0 + 31 of C from the staging
-// block: + C when beta, then the bias and clamp epilogue.
+// block: unscaled by 2^-(e_row + e_col), + C when beta, then the bias and
+// clamp epilogue.
 __device__ __forceinline__ void flush_block(const float4* sw, int lane, int wrow0, int col0, int M, int N, bool vec,
-                                            int beta, const Epilogue& ep, float* __restrict__ C) {
+                                            int beta, const Epilogue& ep, const int* __restrict__ eA,
+                                            const int* __restrict__ eB, float* __restrict__ C) {
   const int j = lane & 7, col = col0 + 4 * j;
+  // eB holds n exponents in a buffer padded to 64: the lanes past n read
+  // padding, and their columns are never stored
+  const int4 ec = col < N ? __ldg(reinterpret_cast<const int4*>(eB + col)) : make_int4(0, 0, 0, 0);
 #pragma unroll 1
   for (int i = 0; i < 8; ++i) {
     const int r = i * 4 + (lane >> 3), grow = wrow0 + r;
-    float4 o = sw[r * 8 + (j ^ (r & 7))];
     if (grow >= M || col >= N) continue;
+    const float4 raw = sw[r * 8 + (j ^ (r & 7))];
+    const int erow = __ldg(eA + grow);
+    float4 o = make_float4(pow2_scale(raw.x, -(erow + ec.x)), pow2_scale(raw.y, -(erow + ec.y)),
+                           pow2_scale(raw.z, -(erow + ec.z)), pow2_scale(raw.w, -(erow + ec.w)));
     if (!vec) {  // a row pitch that is not a multiple of 16 bytes
       float* dst = C + (int64_t)grow * N + col;
       const float ov[4] = {o.x, o.y, o.z, o.w};
@@ -1044,7 +1049,6 @@ __global__ void __launch_bounds__(kThreadsP, 1)
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev == (unsigned)(splits - 1) && ok) {
           __threadfence();
-          const int erow = row < M ? __ldg(eA + row) : 0;
           const int c0 = n0 + h * 128;
           const int wrow0 = m0 + (int)rank * 128 + q * 32;
           float4* sw = epi_stage + (warp - 2) * 256;
@@ -1062,26 +1066,24 @@ __global__ void __launch_bounds__(kThreadsP, 1)
                 a.z = __fadd_rn(a.z, b.z);
                 a.w = __fadd_rn(a.w, b.w);
               }
-              stage_quad(sw, lane, j, a, erow, eB, c0 + cc + 4 * j, N);
+              stage_quad(sw, lane, j, a);
             }
             __syncwarp();
-            flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, C);
+            flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, eA, eB, C);
             __syncwarp();
           }
         }
       } else if (ok) {
         const int c0 = n0 + h * 128;
         const int wrow0 = m0 + (int)rank * 128 + q * 32;
-        const int erow = row < M ? __ldg(eA + row) : 0;
         float4* sw = epi_stage + (warp - 2) * 256;
 #pragma unroll
         for (int cc = 0; cc < 128; cc += 32) {
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            stage_quad(sw, lane, j, make_float4(v[cc + 4 * j], v[cc + 4 * j + 1], v[cc + 4 * j + 2], v[cc + 4 * j + 3]),
-                       erow, eB, c0 + cc + 4 * j, N);
+            stage_quad(sw, lane, j, make_float4(v[cc + 4 * j], v[cc + 4 * j + 1], v[cc + 4 * j + 2], v[cc + 4 * j + 3]));
           __syncwarp();
-          flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, C);
+          flush_block(sw, lane, wrow0, c0 + cc, M, N, vec, beta, ep, eA, eB, C);
           __syncwarp();
         }
       }
