@@ -380,7 +380,8 @@ def test_gemm_f32_c4_sizes(cuda, mkn, tol):
 
 
 @pytest.mark.parametrize("mkn,splits", [((4096, 8192, 4096), None), ((4096, 1024, 4096), "2"),
-                                        ((8192, 4096, 1000), "3"), ((2048, 4096, 1000), "4")])
+                                        ((8192, 4096, 1000), "3"), ((2048, 4096, 1000), "4"),
+                                        ((1024, 4096, 1001), "2")])
 def test_gemm_f32_split_k_deterministic(cuda, mkn, splits, monkeypatch):
     """Split K (chosen by the heuristic when splits is None, else forced with
     the tuning override): the last-arriving unit sums the partials in split

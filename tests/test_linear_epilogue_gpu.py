@@ -23,7 +23,8 @@ def _dev(torch, a):
 
 # shapes for the CTA-pair kernel (m >= 256), the single-CTA kernel (64 <= m < 256),
 # the SIMT fallback (small), odd n (not a multiple of 4) and padded k
-@pytest.mark.parametrize("mkn", [(512, 384, 1000), (128, 256, 512), (300, 200, 260), (32, 64, 10), (8192, 512, 256)])
+@pytest.mark.parametrize("mkn", [(512, 384, 1000), (128, 256, 512), (300, 200, 260), (300, 200, 257), (32, 64, 10),
+                                 (8192, 512, 256)])
 @pytest.mark.parametrize("trans", [(0, 0), (1, 0), (0, 1)])
 @pytest.mark.parametrize("act", ["bias", "bias_relu", "relu_only", "clamp_range"])
 def test_gemm_bias_act_matches_eager_ops(cuda, mkn, trans, act):
